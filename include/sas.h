@@ -1,0 +1,179 @@
+/*
+ * sas.h -- C ABI of the B200 (sm_100a) sparse shared-KV attention library
+ * (libsas.so).  Plain pointers and sizes only; no framework types.
+ *
+ * Reference interfaces each entry point replaces (file:line in the reference
+ * project yangqiang2018/sparse_attn_sharedkv):
+ *
+ *   sas_fwd / sas_fwd_workspace_size
+ *       the device call api.py:372-384 (the TileLang jit function built by
+ *       kernel.py:73-183 with the 11-tensor signature kernel.py:356-382) and
+ *       its twin sparse_flash_mla/sparse_flash_mla_api.py:231-242; the
+ *       runtime-owned workspaces of the reference (workspace_idx) become a
+ *       caller-owned buffer sized by sas_fwd_workspace_size.
+ *   sas_combine
+ *       the split-KV (flash-decode) reduction that the reference plans in
+ *       metadata.py:795-827, 925-954 (fdMetadata) but never runs.
+ *   sas_metadata
+ *       metadata.py:1018-1086 (sparse_attn_sharedkv_metadata), the port of the
+ *       aicpu SparseAttnSharedkvMetadata scheduler; bit-exact int32[1024].
+ *   sas_plan_size / sas_plan
+ *       the B200 work split that takes the place of the 24/36-core metadata
+ *       table for 148 SMs (split-KV pieces + combine bookkeeping).
+ *   sas_error_string / sas_version
+ *       error reporting in place of the reference's Python asserts
+ *       (api.py:187-191, 279-282).
+ *
+ * Conventions: every function returns SAS_OK (0) or a positive SAS_ERR_*
+ * code.  Device pointers are marked [device]; everything else is host memory.
+ * Streams are passed as `void*` (a cudaStream_t; NULL = legacy default).
+ * The library allocates no device memory: outputs and workspace belong to
+ * the caller.
+ */
+#ifndef SAS_H_
+#define SAS_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---- */
+enum {
+  SAS_OK = 0,
+  SAS_ERR_INVALID = 1,      /* bad argument: shape, mode, null pointer, size   */
+  SAS_ERR_UNSUPPORTED = 2,  /* valid in the reference API but not built here   */
+  SAS_ERR_CUDA = 3,         /* a CUDA runtime call or kernel launch failed      */
+  SAS_ERR_SCHEDULE = 4,     /* the scheduler could not finish (see sas_metadata)*/
+  SAS_ERR_WORKSPACE = 5,    /* workspace missing, misaligned or too small       */
+  SAS_ERR_DEVICE = 6        /* a device-side check fired (see SasFwdParams.err) */
+};
+
+/* ---- layouts / modes / dtypes (values of the reference's string enums) ---- */
+enum { SAS_LAYOUT_BSND = 0, SAS_LAYOUT_TND = 1, SAS_LAYOUT_BSH = 2, SAS_LAYOUT_BNSD = 3,
+       SAS_LAYOUT_PA_ND = 4 };
+enum { SAS_DTYPE_BF16 = 0, SAS_DTYPE_FP16 = 1 };
+/* Scenario (api.py:196-202): 1 = SWA, 2 = CFA (dense compressed), 3 = SCFA (top-k). */
+enum { SAS_SCENARIO_SWA = 1, SAS_SCENARIO_CFA = 2, SAS_SCENARIO_SCFA = 3 };
+
+/* ---- reference metadata table geometry (metadata.py:38-60) ---- */
+#define SAS_META_SIZE 1024
+#define SAS_AIC_CORE_NUM 36
+#define SAS_AIV_CORE_NUM 72
+#define SAS_FA_METADATA_SIZE 8
+#define SAS_FD_METADATA_SIZE 8
+
+/* Parameters of sas_metadata: the keyword arguments of
+ * sparse_attn_sharedkv_metadata (metadata.py:1018-1045).  Optional tensors are
+ * (pointer, length) pairs; length 0 means "None / empty". */
+typedef struct SasMetaParams {
+  int64_t num_heads_q, num_heads_kv, head_dim;
+  const int64_t* cu_seqlens_q;      int64_t n_cu_seqlens_q;
+  const int64_t* cu_seqlens_ori_kv; int64_t n_cu_seqlens_ori_kv;
+  const int64_t* cu_seqlens_cmp_kv; int64_t n_cu_seqlens_cmp_kv;
+  const int64_t* seqused_q;         int64_t n_seqused_q;
+  const int64_t* seqused_kv;        int64_t n_seqused_kv;
+  int64_t batch_size, max_seqlen_q, max_seqlen_kv;
+  int64_t ori_topk, cmp_topk, cmp_ratio;
+  int32_t ori_mask_mode, cmp_mask_mode;
+  int64_t ori_win_left, ori_win_right;
+  int32_t layout_q, layout_kv;      /* SAS_LAYOUT_* */
+  int32_t has_ori_kv, has_cmp_kv;
+  int64_t aic_core_num, aiv_core_num;
+} SasMetaParams;
+
+/* Reference-exact scheduler (host).  Writes SAS_META_SIZE int32 to `out`.
+ * Replaces metadata.py:1018-1086. */
+int sas_metadata(const SasMetaParams* params, int32_t* out, size_t out_len);
+
+/* ---- forward ---- */
+
+/* Problem description shared by the planner and the forward.  Host arrays. */
+typedef struct SasProblem {
+  int32_t batch;            /* B                                               */
+  int32_t layout_q;         /* SAS_LAYOUT_TND or SAS_LAYOUT_BSND                */
+  int32_t max_q_len;        /* S (BSND row stride in tokens); ignored for TND   */
+  int32_t total_tokens;     /* rows of q: T (TND) or B*S (BSND)                 */
+  const int32_t* q_start;   /* [B] flat token offset of batch b (q_prefix)       */
+  const int32_t* q_len;     /* [B] valid query tokens of batch b (act_q)         */
+  const int32_t* kv_len;    /* [B] seqused_kv                                    */
+  int32_t num_heads;        /* N1 (1..128), one KV head                         */
+  int32_t scenario;         /* SAS_SCENARIO_*                                   */
+  int32_t ori_win_left;     /* window is [s_g - left, s_g]; -1 = empty window   */
+  int32_t cmp_ratio;        /* compression ratio (>= 1) for scenarios 2, 3      */
+  int32_t topk;             /* K of cmp_indices (scenario 3)                    */
+} SasProblem;
+
+/* Device-side buffers and remaining shapes of one forward call. */
+typedef struct SasFwdParams {
+  const void* q;                   /* [device] [total_tokens, H, d_qk] dtype      */
+  const void* ori_kv;              /* [device] [ori_blocks, ori_bs, 1, d_qk]      */
+  const int32_t* ori_block_table;  /* [device] [B, ori_table_len]                 */
+  const void* cmp_kv;              /* [device] or NULL (scenario 1)               */
+  const int32_t* cmp_block_table;  /* [device] [B, cmp_table_len] or NULL         */
+  const int32_t* cmp_indices;      /* [device] [total_tokens, topk] or NULL       */
+  const float* sinks;              /* [device] [H] fp32                           */
+  void* out;                       /* [device] [total_tokens, H, d_v] dtype       */
+  float* lse;                      /* [device] [total_tokens, H] fp32             */
+  int32_t* err;                    /* [device] optional int32[4] error record     */
+  int32_t head_dim;                /* d_qk: 512 or 576                            */
+  int32_t head_dim_v;              /* d_v: 512                                    */
+  int32_t dtype;                   /* SAS_DTYPE_*                                 */
+  float softmax_scale;
+  int32_t ori_block_size, ori_num_blocks, ori_table_len;
+  int32_t cmp_block_size, cmp_num_blocks, cmp_table_len;
+  int32_t num_sms;                 /* persistent workers (0 = all SMs)            */
+} SasFwdParams;
+
+/* Bytes of device workspace a forward call needs (plan + split-KV partials).
+ * Host-only; deterministic in (problem, num_sms). */
+int sas_fwd_workspace_size(const SasProblem* prob, int32_t num_sms, size_t* bytes);
+
+/* Full forward on `stream`: plans on the host, uploads the plan into the
+ * workspace (cudaMemcpyAsync), runs the attention kernel and, when a query
+ * row was split across SMs, the LSE-combine kernel.  Replaces api.py:372-384.
+ * `workspace` must be 256-byte aligned and at least sas_fwd_workspace_size. */
+int sas_fwd(const SasProblem* prob, const SasFwdParams* params, void* workspace,
+            size_t workspace_bytes, void* stream);
+
+/* LSE-combine of split-KV partials (normally called by sas_fwd).  For each of
+ * `num_rows` split rows, piece i of row r is partial slot `partial_base[r]+i`:
+ * o_partial [slots, H, d_v] fp32 (normalised), lse_partial [slots, H] fp32.
+ * Writes out [token, H, d_v] dtype and lse [token, H].  All pointers device. */
+int sas_combine(const int32_t* row_token, const int32_t* row_pieces,
+                const int32_t* partial_base, int32_t num_rows, const float* o_partial,
+                const float* lse_partial, int32_t num_heads, int32_t head_dim_v, int32_t dtype,
+                void* out, float* lse, void* stream);
+
+/* ---- B200 work plan (host) ---- */
+
+/* Plan summary returned by sas_plan (sizes in elements). */
+typedef struct SasPlanInfo {
+  int32_t num_rows;          /* work rows (query tokens incl. padded BSND rows) */
+  int32_t num_workers;       /* persistent workers (CTA groups)                 */
+  int32_t head_groups;       /* CTAs per worker = ceil(H / 64)                  */
+  int32_t num_split_rows;    /* rows whose keys were split across workers       */
+  int32_t num_partials;      /* partial slots used by split rows                */
+  int64_t total_tiles;       /* 64-key tiles over all rows                      */
+  int64_t plan_ints;         /* int32 entries of the serialised plan            */
+} SasPlanInfo;
+
+/* Size the plan (host). */
+int sas_plan_size(const SasProblem* prob, int32_t num_sms, SasPlanInfo* info);
+/* Build the plan into `plan` (host int32[info.plan_ints]). */
+int sas_plan(const SasProblem* prob, int32_t num_sms, int32_t* plan, int64_t plan_len,
+             SasPlanInfo* info);
+
+/* ---- misc ---- */
+const char* sas_error_string(int code);
+const char* sas_version(void);
+/* Number of SMs of the current device (0 if no device). */
+int32_t sas_device_sm_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SAS_H_ */

@@ -1,0 +1,767 @@
+// Sparse shared-KV attention forward for B200 (sm_100a): tcgen05 + TMEM.
+//
+// One persistent CTA per SM owns 64 query heads of a "worker" span of the
+// plan (sas_plan.cpp): a contiguous run of (query token, 64-key tile) units.
+// Calls with more than 64 heads use two CTAs per worker, one per head group;
+// the pair walks the same tiles at the same time, so the second read of
+// every key row is an L2 hit.
+//
+// Per tile of 64 key slots (window keys then compressed keys, golden.py
+// tile order) the CTA runs:
+//
+//   producer warps (2)  slot -> (cache, logical pos) -> block table -> row;
+//                       cp.async 16 B granules into a 128B-swizzled K tile
+//                       (paged window load, kernel.py:3580-3600, and top-k
+//                       gather, kernel.py:2606-2751), -1 stop / threshold
+//                       masks (golden.py:28-66) into a per-tile valid mask
+//   MMA warp (1 lane)   S = Q K^T  : 36 x tcgen05.mma.ws M64 N64 K16 (d_qk 576)
+//                       O += P V   : 8 x tcgen05.mma.ws M64 N256 K16, where V is
+//                                    the same smem K tile read MN-major (d_v 512)
+//   softmax warps (4)   tcgen05.ld of S, mask, scale, online softmax seeded
+//                       by the sink (golden.py:156-196) in the exp2 domain,
+//                       P rounded to the input dtype into smem, lazy O
+//                       rescale in TMEM, final O / l and LSE (kernel.py:3110-3245)
+//
+// TMEM (512 columns): O[64 x 512] fp32 as two .ws M64 N256 accumulators
+// (cols 0-255, all 128 lanes), S[64 x 64] fp32 double-buffered (cols 256-319).
+// Shared memory: Q 72 KB, two K stages of 72 KB, P 8 KB.
+//
+// Every wait on an mbarrier is bounded: on timeout the thread records an
+// error in the caller's error word, raises the CTA abort flag and leaves its
+// loop; no trap, no unbounded spin.
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "sas.h"
+#include "sas_internal.h"
+#include "sas_kernels.h"
+
+namespace sas {
+namespace {
+
+constexpr int kNumSoftmaxWarps = 4;
+constexpr int kProducerWarp0 = 4;
+constexpr int kNumProducerWarps = 2;
+constexpr int kMmaWarp = 6;
+constexpr int kThreads = 32 * 7;
+constexpr int kProducerThreads = 32 * kNumProducerWarps;
+constexpr int kSoftmaxThreads = 32 * kNumSoftmaxWarps;
+
+constexpr int kMaxChunks = 9;                   // d_qk / 64
+constexpr int kChunkBytes = kHeadsPerCta * 128;  // 64 rows x 64 bf16 = 8 KB
+constexpr int kQBytes = kMaxChunks * kChunkBytes;
+constexpr int kStageBytes = kMaxChunks * kChunkBytes;
+constexpr int kPBytes = kHeadsPerCta * kTileKeys * 2;
+constexpr int kSmemQ = 0;
+constexpr int kSmemK0 = kSmemQ + kQBytes;
+constexpr int kSmemP = kSmemK0 + 2 * kStageBytes;
+constexpr int kSmemTiles = kSmemP + kPBytes;       // 229376
+constexpr int kSmemDynamic = kSmemTiles + 1024;    // + runtime 1 KB alignment slack
+
+// TMEM columns.
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemO = 0;     // O[:, 0:256) at +0, O[:, 256:512) at +128
+constexpr uint32_t kTmemS = 256;   // S buffers at +256, +288
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kRescaleThreshold = 8.0f;  // lazy O rescale (log2 units)
+
+constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 2 GHz
+
+// ---------------------------------------------------------------------------
+// PTX helpers.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+      : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem], weight-stationary form (M = 64 uses all
+// 128 TMEM lanes: columns [0, N/2) on lanes 0-63, [N/2, N) on lanes 64-127).
+__device__ __forceinline__ void mma_ws(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.ws.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 32 consecutive 32-bit columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+      "%28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+      "%28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle (sm_100 version 1).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Instruction descriptor of kind::f16 with fp32 accumulation.
+__host__ __device__ constexpr uint32_t instr_desc(int m, int n, bool bf16, bool a_mn, bool b_mn) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
+         ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(m >> 4) << 24);
+}
+
+// Byte offset of (row, 16-byte granule) inside a 128B-swizzled [rows x 64]
+// 16-bit chunk: rows are 128 B apart, granules XOR-permuted by row % 8.
+__device__ __forceinline__ uint32_t swz(int row, int granule) {
+  return (uint32_t)(row * 128 + ((granule ^ (row & 7)) << 4));
+}
+
+struct Ctl {
+  uint64_t kv_full[2];
+  uint64_t kv_empty[2];
+  uint64_t q_full, q_empty;
+  uint64_t s_full[2];
+  uint64_t s_empty[2];
+  uint64_t p_full, pv_done, o_free, drain;
+  uint64_t xbar[2];               // softmax partner exchange (bounded, no bar.sync)
+  uint32_t tmem_base;
+  volatile int abort;
+  uint32_t valid[2][2];          // per stage, per half: 32 slot bits
+  float red[2][2][kHeadsPerCta];  // [parity][half][row]: partner exchange
+};
+
+struct Row {
+  int token, b, s, slots, flags, first_worker, partial_base, window;
+};
+
+__device__ __forceinline__ Row load_row(const int* rows, int r) {
+  const int4* p = reinterpret_cast<const int4*>(rows + (size_t)r * kRowInts);
+  int4 a = __ldg(p), c = __ldg(p + 1);
+  return Row{a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+}
+
+__device__ void record_error(int* err, int code, int site, int detail) {
+  if (err != nullptr && atomicCAS(err, 0, code) == 0) {
+    err[1] = site;
+    err[2] = detail;
+    err[3] = (int)blockIdx.x;
+  }
+}
+
+// Bounded wait; on timeout records the error and raises the CTA abort flag.
+__device__ __forceinline__ bool wait_bar(Ctl* ctl, uint64_t* bar, uint32_t parity, int* err,
+                                         int site) {
+  const uint32_t a = smem_addr(bar);
+  if (mbar_try_wait(a, parity)) return true;
+  long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait(a, parity)) return true;
+    if (ctl->abort) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      record_error(err, SAS_ERR_DEVICE, site, (int)parity);
+      ctl->abort = 1;
+      return false;
+    }
+  }
+}
+
+template <bool kBf16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  if constexpr (kBf16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+
+// Iterate over the (row, tile range) segments of this CTA's worker span.
+struct Span {
+  int r0, t0, r1, t1, piece0;
+};
+
+__device__ __forceinline__ Span load_span(const int* plan, int worker) {
+  const int* w = plan + plan[H_WORKERS_OFF] + worker * kWorkerInts;
+  return Span{__ldg(w), __ldg(w + 1), __ldg(w + 2), __ldg(w + 3), __ldg(w + 4)};
+}
+
+__device__ __forceinline__ int row_tiles(const Row& rv) {
+  return (rv.slots + kTileKeys - 1) / kTileKeys;
+}
+
+// ---------------------------------------------------------------------------
+// The kernel.
+// ---------------------------------------------------------------------------
+
+template <bool kBf16>
+__global__ void __launch_bounds__(kThreads, 1) sas_fwd_kernel(const FwdArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ Ctl ctl;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int hg = args.head_groups;
+  const int worker = blockIdx.x / hg;
+  const int group = blockIdx.x % hg;
+  const int* plan = args.plan;
+  const int* rows = plan + plan[H_ROWS_OFF];
+  const int nchunks = args.head_dim >> 6;
+  int* err = args.err;
+
+  // 1024-byte aligned tile area.
+  const uint32_t raw = smem_addr(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t sQ = base + kSmemQ;
+  const uint32_t sK0 = base + kSmemK0;
+  const uint32_t sP = base + kSmemP;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_addr(&ctl.kv_full[i]), 2 * kProducerThreads);
+      mbar_init(smem_addr(&ctl.kv_empty[i]), 1);
+      mbar_init(smem_addr(&ctl.s_full[i]), 1);
+      mbar_init(smem_addr(&ctl.s_empty[i]), kSoftmaxThreads);
+    }
+    mbar_init(smem_addr(&ctl.q_full), kProducerThreads);
+    mbar_init(smem_addr(&ctl.q_empty), 1);
+    mbar_init(smem_addr(&ctl.p_full), kSoftmaxThreads);
+    mbar_init(smem_addr(&ctl.pv_done), 1);
+    mbar_init(smem_addr(&ctl.o_free), kSoftmaxThreads);
+    mbar_init(smem_addr(&ctl.drain), 1);
+    mbar_init(smem_addr(&ctl.xbar[0]), kSoftmaxThreads);
+    mbar_init(smem_addr(&ctl.xbar[1]), kSoftmaxThreads);
+    ctl.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == kMmaWarp) {
+    asm volatile(
+        "tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+            smem_addr(&ctl.tmem_base)),
+        "r"(kTmemCols)
+        : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl.tmem_base;
+
+  const Span span = (worker < plan[H_NUM_WORKERS]) ? load_span(plan, worker) : Span{-1, 0, -1, 0, 0};
+
+  if (warp >= kProducerWarp0 && warp < kProducerWarp0 + kNumProducerWarps) {
+    // ======================= producers =======================
+    const int pw = warp - kProducerWarp0;
+    const int D = args.head_dim;
+    const int gran = D >> 3;  // 16-byte granules per row
+    const char* qbase = reinterpret_cast<const char*>(args.q);
+    uint32_t kv_empty_par[2] = {1u, 1u};
+    uint32_t q_empty_par = 1u;
+    int stage = 0;
+    bool ok = true;
+    for (int r = span.r0; ok && span.r0 >= 0 && r <= span.r1; ++r) {
+      const Row rv = load_row(rows, r);
+      const int tiles = row_tiles(rv);
+      const int ja = (r == span.r0) ? span.t0 : 0;
+      const int jb = (r == span.r1) ? span.t1 : (tiles > 0 ? tiles : 1);
+      if (tiles == 0 || ja >= jb) continue;
+      // ---- Q tile: 64 heads of this group ----
+      if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.q_empty, q_empty_par, err, 1))) {
+        ok = false;
+        break;
+      }
+      q_empty_par ^= 1u;
+      for (int hh = 0; hh < 32; ++hh) {
+        const int h = pw * 32 + hh;
+        const int head = group * kHeadsPerCta + h;
+        const bool live = head < args.num_heads;
+        const char* src = qbase + ((size_t)rv.token * args.num_heads + (live ? head : 0)) *
+                                      (size_t)D * 2;
+        for (int gi = lane; gi < gran; gi += 32) {
+          const uint32_t dst = sQ + (gi >> 3) * kChunkBytes + swz(h, gi & 7);
+          cp_async_16(dst, src + gi * 16, live ? 16u : 0u);
+        }
+      }
+      cp_async_arrive_noinc(smem_addr(&ctl.q_full));
+
+      // ---- key tiles ----
+      const int act_q = args.q_len[rv.b];
+      const int act_kv = args.kv_len[rv.b];
+      const QueryKeys qk = query_keys(args.scenario, act_q, act_kv, rv.s, args.ori_win_left,
+                                      args.cmp_ratio, args.topk);
+      const int W = rv.window;
+      const int* idx_row = (args.scenario == SAS_SCENARIO_SCFA)
+                               ? args.cmp_indices + (size_t)rv.token * args.topk
+                               : nullptr;
+      // Slots before this piece may hold a -1 that stops the scan.
+      bool stopped = false;
+      if (idx_row != nullptr && ja > 0) {
+        const int lim = min(ja * kTileKeys - W, qk.cmp);
+        for (int c0 = 0; c0 < lim && !stopped; c0 += 32) {
+          const int c = c0 + lane;
+          const bool m1 = (c < lim) && (__ldg(idx_row + c) == -1);
+          stopped = __any_sync(0xffffffffu, m1);
+        }
+      }
+      for (int j = ja; j < jb; ++j) {
+        if (!__all_sync(0xffffffffu,
+                        wait_bar(&ctl, &ctl.kv_empty[stage], kv_empty_par[stage], err, 2))) {
+          ok = false;
+          break;
+        }
+        kv_empty_par[stage] ^= 1u;
+        // -1 positions among the compressed slots of this tile (both warps
+        // scan the whole tile so the stop prefix needs no cross-warp sync).
+        uint64_t m1mask = 0;
+        if (idx_row != nullptr) {
+          const int ca = j * kTileKeys + lane - W;
+          const int cb = ca + 32;
+          const bool ma = (ca >= 0 && ca < qk.cmp) && (__ldg(idx_row + ca) == -1);
+          const bool mb = (cb >= 0 && cb < qk.cmp) && (__ldg(idx_row + cb) == -1);
+          m1mask = (uint64_t)__ballot_sync(0xffffffffu, ma) |
+                   ((uint64_t)__ballot_sync(0xffffffffu, mb) << 32);
+        }
+        // My slot: key = pw*32 + lane.
+        const int key = pw * 32 + lane;
+        const int slot = j * kTileKeys + key;
+        bool valid = false;
+        const char* src = nullptr;
+        if (slot < W) {
+          const int pos = qk.win_lo + slot;
+          const int lb = pos / args.ori_block_size;
+          valid = true;
+          if (lb < args.ori_table_len) {
+            const int blk = __ldg(args.ori_block_table + (size_t)rv.b * args.ori_table_len + lb);
+            if (blk >= 0 && blk < args.ori_num_blocks) {
+              src = reinterpret_cast<const char*>(args.ori_kv) +
+                    ((size_t)blk * args.ori_block_size + (pos - lb * args.ori_block_size)) *
+                        (size_t)D * 2;
+            } else if (blk >= args.ori_num_blocks) {
+              record_error(err, SAS_ERR_DEVICE, 10, blk);
+            }
+          } else {
+            record_error(err, SAS_ERR_DEVICE, 11, pos);
+          }
+        } else if (slot < rv.slots) {
+          const int c = slot - W;
+          int pos = c;
+          valid = true;
+          if (idx_row != nullptr) {
+            pos = __ldg(idx_row + c);
+            const bool before = stopped || ((m1mask & ((1ull << key) - 1ull)) != 0);
+            valid = !before && pos >= 0 && pos < qk.thr;
+          }
+          if (valid) {
+            const int lb = pos / args.cmp_block_size;
+            if (lb < args.cmp_table_len) {
+              const int blk =
+                  __ldg(args.cmp_block_table + (size_t)rv.b * args.cmp_table_len + lb);
+              if (blk >= 0 && blk < args.cmp_num_blocks) {
+                src = reinterpret_cast<const char*>(args.cmp_kv) +
+                      ((size_t)blk * args.cmp_block_size + (pos - lb * args.cmp_block_size)) *
+                          (size_t)D * 2;
+              } else if (blk >= args.cmp_num_blocks) {
+                record_error(err, SAS_ERR_DEVICE, 12, blk);
+              }
+            } else {
+              record_error(err, SAS_ERR_DEVICE, 13, pos);
+            }
+          }
+        }
+        if (m1mask != 0) stopped = true;
+        const uint32_t vbits = __ballot_sync(0xffffffffu, valid);
+        if (lane == 0) ctl.valid[stage][pw] = vbits;
+        __syncwarp();
+        mbar_arrive(smem_addr(&ctl.kv_full[stage]));
+        // Copy the 32 rows of this warp; zero rows where there is no source.
+        const uint32_t sK = sK0 + stage * kStageBytes;
+        for (int k = 0; k < 32; ++k) {
+          const char* s = reinterpret_cast<const char*>(
+              __shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(src), k));
+          const int row = pw * 32 + k;
+          const uint32_t nbytes = (s != nullptr) ? 16u : 0u;
+          const char* s_safe = (s != nullptr) ? s : reinterpret_cast<const char*>(args.ori_kv);
+          for (int gi = lane; gi < gran; gi += 32) {
+            cp_async_16(sK + (gi >> 3) * kChunkBytes + swz(row, gi & 7), s_safe + gi * 16,
+                        nbytes);
+          }
+        }
+        cp_async_arrive_noinc(smem_addr(&ctl.kv_full[stage]));
+        stage ^= 1;
+      }
+    }
+    cp_async_wait_all();
+  } else if (warp == kMmaWarp) {
+    // ======================= MMA issuer =======================
+    if (lane == 0) {
+      const uint32_t idesc_qk = instr_desc(64, 64, kBf16, false, false);
+      const uint32_t idesc_pv = instr_desc(64, 256, kBf16, false, true);
+      uint32_t kv_full_par[2] = {0u, 0u};
+      uint32_t s_empty_par[2] = {1u, 1u};
+      uint32_t q_full_par = 0u, p_full_par = 0u, o_free_par = 1u;
+      int stage = 0, sbuf = 0;
+      bool ok = true;
+
+      auto issue_qk = [&](int st, int sb) -> bool {
+        if (!wait_bar(&ctl, &ctl.kv_full[st], kv_full_par[st], err, 20)) return false;
+        kv_full_par[st] ^= 1u;
+        if (!wait_bar(&ctl, &ctl.s_empty[sb], s_empty_par[sb], err, 21)) return false;
+        s_empty_par[sb] ^= 1u;
+        fence_proxy_async();
+        tc_fence_after();
+        const uint32_t d = tmem + kTmemS + 32u * sb;
+        const uint32_t kb = sK0 + st * kStageBytes;
+        for (int c = 0; c < nchunks; ++c) {
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint64_t a = smem_desc(sQ + c * kChunkBytes + ks * 32, 16, 1024);
+            const uint64_t b = smem_desc(kb + c * kChunkBytes + ks * 32, 16, 1024);
+            mma_ws(d, a, b, idesc_qk, (c | ks) != 0 ? 1u : 0u);
+          }
+        }
+        tc_commit(smem_addr(&ctl.s_full[sb]));
+        return true;
+      };
+
+      for (int r = span.r0; ok && span.r0 >= 0 && r <= span.r1; ++r) {
+        const Row rv = load_row(rows, r);
+        const int tiles = row_tiles(rv);
+        const int ja = (r == span.r0) ? span.t0 : 0;
+        const int jb = (r == span.r1) ? span.t1 : (tiles > 0 ? tiles : 1);
+        if (tiles == 0 || ja >= jb) continue;
+        if (!wait_bar(&ctl, &ctl.q_full, q_full_par, err, 22)) { ok = false; break; }
+        q_full_par ^= 1u;
+        int st_next = stage, sb_next = sbuf;
+        if (!issue_qk(st_next, sb_next)) { ok = false; break; }
+        if (jb - ja == 1) tc_commit(smem_addr(&ctl.q_empty));
+        for (int j = ja; j < jb; ++j) {
+          const int st = stage, sb = sbuf;
+          stage ^= 1;
+          sbuf ^= 1;
+          if (j + 1 < jb) {
+            if (!issue_qk(stage, sbuf)) { ok = false; break; }
+            if (j + 2 == jb) tc_commit(smem_addr(&ctl.q_empty));
+          }
+          if (!wait_bar(&ctl, &ctl.p_full, p_full_par, err, 23)) { ok = false; break; }
+          p_full_par ^= 1u;
+          if (j == ja) {
+            if (!wait_bar(&ctl, &ctl.o_free, o_free_par, err, 24)) { ok = false; break; }
+            o_free_par ^= 1u;
+          }
+          fence_proxy_async();
+          tc_fence_after();
+          const uint32_t kb = sK0 + st * kStageBytes;
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint64_t a = smem_desc(sP + ks * 32, 16, 1024);
+            for (int hv = 0; hv < 2; ++hv) {
+              const uint64_t b =
+                  smem_desc(kb + (4 * hv) * kChunkBytes + ks * 2048, kChunkBytes, 1024);
+              mma_ws(tmem + kTmemO + 128u * hv, a, b, idesc_pv,
+                     (j == ja && ks == 0) ? 0u : 1u);
+            }
+          }
+          tc_commit(smem_addr(&ctl.kv_empty[st]));
+          tc_commit(smem_addr(&ctl.pv_done));
+          (void)sb;
+        }
+      }
+      // Drain: the commit arrives once every MMA issued above has finished,
+      // so TMEM is never released under an in-flight MMA (also on abort).
+      tc_commit(smem_addr(&ctl.drain));
+      wait_bar(&ctl, &ctl.drain, 0u, err, 25);
+    }
+    __syncwarp();
+  } else if (warp < kNumSoftmaxWarps) {
+    // ======================= softmax / epilogue =======================
+    const int L = threadIdx.x;           // TMEM lane 0..127
+    const int m = L & (kHeadsPerCta - 1);  // head row inside the group
+    const int half = L >> 6;             // key half / output half
+    const int head = group * kHeadsPerCta + m;
+    const bool live = head < args.num_heads;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const float c2 = args.softmax_scale * kLog2e;
+    const float sink = live ? __ldg(args.sinks + head) : -INFINITY;
+    uint32_t kv_full_par[2] = {0u, 0u};
+    uint32_t s_full_par[2] = {0u, 0u};
+    uint32_t pv_done_par = 0u;
+    uint32_t xph[2] = {0u, 0u};
+    int stage = 0, sbuf = 0, xpar = 0;
+    // Partner exchange through ctl.red[xpar], ordered by the bounded
+    // mbarrier ctl.xbar[xpar] (all 128 softmax threads arrive, then wait).
+    auto exchange = [&](int site) -> bool {
+      mbar_arrive(smem_addr(&ctl.xbar[xpar]));
+      const bool w = wait_bar(&ctl, &ctl.xbar[xpar], xph[xpar], err, site);
+      xph[xpar] ^= 1u;
+      return w;
+    };
+    bool ok = true;
+    const int dv = args.head_dim_v;
+
+    for (int r = span.r0; ok && span.r0 >= 0 && r <= span.r1; ++r) {
+      const Row rv = load_row(rows, r);
+      const int tiles = row_tiles(rv);
+      const int ja = (r == span.r0) ? span.t0 : 0;
+      const int jb = (r == span.r1) ? span.t1 : (tiles > 0 ? tiles : 1);
+      if (ja >= jb) continue;
+      const size_t orow = (size_t)rv.token * args.num_heads + head;
+      if (tiles == 0) {
+        // No key slot: out = 0, lse = sink (golden.py:162-200), padded rows 0.
+        if (live) {
+          uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<char*>(args.out) +
+                                              (orow * dv + half * (dv / 2)) * 2);
+          for (int i = 0; i < dv / 16; ++i) o[i] = make_uint4(0, 0, 0, 0);
+          if (half == 0) args.lse[orow] = (rv.flags & kRowPadded) ? 0.f : sink;
+        }
+        continue;
+      }
+      const bool first_piece = (ja == 0);
+      float m_run = first_piece ? sink * kLog2e : -INFINITY;  // log2 domain
+      float l_run = (first_piece && half == 0) ? 1.f : 0.f;
+      for (int j = ja; j < jb; ++j) {
+        const int st = stage, sb = sbuf;
+        stage ^= 1;
+        sbuf ^= 1;
+        if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.s_full[sb], s_full_par[sb], err, 30))) { ok = false; break; }
+        s_full_par[sb] ^= 1u;
+        if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.kv_full[st], kv_full_par[st], err, 31))) { ok = false; break; }
+        kv_full_par[st] ^= 1u;
+        tc_fence_after();
+        uint32_t sraw[32];
+        tmem_ld32(tmem + lane_off + kTmemS + 32u * sb, sraw);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(smem_addr(&ctl.s_empty[sb]));
+        const uint32_t vb = ctl.valid[st][half];
+        float x[32];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float v = ((vb >> i) & 1u) ? __uint_as_float(sraw[i]) * c2 : -INFINITY;
+          x[i] = v;
+          mx = fmaxf(mx, v);
+        }
+        ctl.red[xpar][half][m] = mx;
+        if (!__all_sync(0xffffffffu, exchange(34))) { ok = false; break; }
+        mx = fmaxf(mx, ctl.red[xpar][half ^ 1][m]);
+        xpar ^= 1;
+        const float m_new = fmaxf(m_run, mx);
+        const bool rescale = (m_new - m_run) > kRescaleThreshold;  // NaN (-inf,-inf) -> false
+        float alpha = 1.f;
+        if (rescale) {
+          alpha = exp2f(m_run - m_new);
+          m_run = m_new;
+          l_run *= alpha;
+        }
+        const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+        float lsum = 0.f;
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float p0 = exp2f(x[i] - m_use);
+          const float p1 = exp2f(x[i + 1] - m_use);
+          lsum += p0 + p1;
+          pk[i / 2] = pack2<kBf16>(p0, p1);
+        }
+        l_run += lsum;
+        if (j > ja) {
+          if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.pv_done, pv_done_par, err, 32))) { ok = false; break; }
+          pv_done_par ^= 1u;
+          tc_fence_after();
+          if (__any_sync(0xffffffffu, rescale)) {
+            // O *= alpha for this thread's 256 accumulator columns.
+            for (int c = 0; c < 8; ++c) {
+              const uint32_t ta = tmem + lane_off + kTmemO + 32u * c;
+              uint32_t v[32];
+              tmem_ld32(ta, v);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+              tmem_st32(ta, v);
+            }
+            tmem_wait_st();
+          }
+        }
+        // P row m, keys [32*half, 32*half + 32) -> granules 4*half .. 4*half+3.
+        uint8_t* prow = gbase + kSmemP;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          uint4 v = make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
+          *reinterpret_cast<uint4*>(prow + swz(m, 4 * half + g)) = v;
+        }
+        fence_proxy_async();
+        tc_fence_before();
+        mbar_arrive(smem_addr(&ctl.p_full));
+      }
+      if (!ok) break;
+      // ---- epilogue of this (row, piece) ----
+      if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.pv_done, pv_done_par, err, 33))) { ok = false; break; }
+      pv_done_par ^= 1u;
+      tc_fence_after();
+      ctl.red[xpar][half][m] = l_run;
+      if (!__all_sync(0xffffffffu, exchange(35))) { ok = false; break; }
+      const float l_tot = l_run + ctl.red[xpar][half ^ 1][m];
+      xpar ^= 1;
+      const bool split = rv.partial_base >= 0;
+      const float inv = (l_tot > 0.f) ? 1.f / l_tot : 0.f;
+      const float lse = (m_run + log2f(l_tot)) * kLn2;
+      for (int c = 0; c < 8; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_off + kTmemO + 32u * c, v);
+        tmem_wait_ld();
+        if (!live) continue;
+        // Column block c: accumulator hv = c / 4, dims hv*256 + half*128 + (c%4)*32.
+        const int d0 = (c >> 2) * 256 + half * 128 + (c & 3) * 32;
+        if (split) {
+          const int piece = (r == span.r0) ? span.piece0 : 0;
+          float* o = args.o_partial +
+                     ((size_t)(rv.partial_base + piece) * args.num_heads + head) * dv + d0;
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            *reinterpret_cast<float4*>(o + i) =
+                make_float4(__uint_as_float(v[i]) * inv, __uint_as_float(v[i + 1]) * inv,
+                            __uint_as_float(v[i + 2]) * inv, __uint_as_float(v[i + 3]) * inv);
+          }
+        } else {
+          uint32_t pkd[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2)
+            pkd[i / 2] = pack2<kBf16>(__uint_as_float(v[i]) * inv, __uint_as_float(v[i + 1]) * inv);
+          uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<char*>(args.out) +
+                                              (orow * dv + d0) * 2);
+#pragma unroll
+          for (int g = 0; g < 4; ++g)
+            o[g] = make_uint4(pkd[4 * g], pkd[4 * g + 1], pkd[4 * g + 2], pkd[4 * g + 3]);
+        }
+      }
+      if (live && half == 0) {
+        if (split) {
+          const int piece = (r == span.r0) ? span.piece0 : 0;
+          args.lse_partial[(size_t)(rv.partial_base + piece) * args.num_heads + head] = lse;
+        } else {
+          args.lse[orow] = lse;
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(smem_addr(&ctl.o_free));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+}  // namespace
+
+int launch_fwd(const FwdArgs& args, int grid, cudaStream_t stream) {
+  static bool configured[2] = {false, false};
+  const bool bf16 = args.dtype == SAS_DTYPE_BF16;
+  const void* fn = bf16 ? (const void*)sas_fwd_kernel<true> : (const void*)sas_fwd_kernel<false>;
+  if (!configured[bf16 ? 0 : 1]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemDynamic);
+    if (e != cudaSuccess) return SAS_ERR_CUDA;
+    configured[bf16 ? 0 : 1] = true;
+  }
+  if (bf16)
+    sas_fwd_kernel<true><<<grid, kThreads, kSmemDynamic, stream>>>(args);
+  else
+    sas_fwd_kernel<false><<<grid, kThreads, kSmemDynamic, stream>>>(args);
+  return cudaGetLastError() == cudaSuccess ? SAS_OK : SAS_ERR_CUDA;
+}
+
+}  // namespace sas

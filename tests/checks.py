@@ -1,0 +1,70 @@
+"""Numerical acceptance criteria used by the parity tests.
+
+* ``check_reference_result`` / ``check_reference_lse``: the reference suite's
+  Ascend-C-style gates (test_sparse_attn_sharedkv.py:394-481): >= 99.5 % of
+  elements within ``np.isclose`` at dtype tolerances and a max normalised
+  relative error < 10 over the failing elements.
+* ``check_north_star``: the benchmark's bf16 gate against an fp32 reference:
+  max |err| <= 2e-2 and mean relative error <= 1e-3 (relative to the mean
+  magnitude of the reference).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+
+def _fulfill(real, expt, rtol, atol):
+    real = np.asarray(real, dtype=np.float32).ravel()
+    expt = np.asarray(expt, dtype=np.float32).ravel()
+    assert real.size == expt.size, f"size mismatch: {real.size} vs {expt.size}"
+    ok = np.isclose(real, expt, rtol=rtol, atol=atol, equal_nan=True)
+    n_err = int((~ok).sum())
+    pct = (real.size - n_err) / max(real.size, 1) * 100.0
+    floor = (1.0 / (1 << 14)) / 0.005
+    b = np.maximum(np.maximum(np.abs(real), np.abs(expt)), floor) + 1e-9
+    with np.errstate(invalid="ignore"):
+        rel = np.abs(real - expt) / b
+    max_rel = float(np.nan_to_num(rel[~ok], nan=np.inf).max()) if n_err else 0.0
+    return pct, max_rel, n_err
+
+
+def check_reference_result(real, expt, dtype: str) -> None:
+    rtol, atol = (0.0078125, 0.0001) if dtype == "bf16" else (0.005, 0.000025)
+    pct, max_rel, n_err = _fulfill(real, expt, rtol, atol)
+    assert pct >= 99.5, f"only {pct:.4f}% within tol ({n_err} failing, max rel {max_rel:.4f})"
+    assert max_rel < 10.0, f"max normalised relative error {max_rel:.4f} >= 10"
+
+
+def check_reference_lse(real, expt, dtype: str) -> None:
+    rtol, atol = (0.015, 0.005) if dtype == "bf16" else (0.01, 0.001)
+    real = np.asarray(real, np.float32)
+    expt = np.asarray(expt, np.float32)
+    fin = np.isfinite(expt)
+    assert np.array_equal(fin, np.isfinite(real)), "lse: -inf pattern differs"
+    assert np.array_equal(real[~fin], expt[~fin])
+    if fin.any():
+        pct, max_rel, n_err = _fulfill(real[fin], expt[fin], rtol, atol)
+        assert pct >= 99.5, f"lse: only {pct:.4f}% within tol ({n_err} failing)"
+        assert max_rel < 10.0, f"lse: max normalised relative error {max_rel:.4f}"
+
+
+def check_north_star(real, expt, max_abs: float = 2e-2, mean_rel: float = 1e-3) -> dict:
+    real = np.asarray(real, np.float32)
+    expt = np.asarray(expt, np.float32)
+    d = np.abs(real - expt)
+    mabs = float(d.max()) if d.size else 0.0
+    mrel = float(d.mean() / max(np.abs(expt).mean(), 1e-12)) if d.size else 0.0
+    assert mabs <= max_abs, f"max abs err {mabs:.3e} > {max_abs}"
+    assert mrel <= mean_rel, f"mean rel err {mrel:.3e} > {mean_rel}"
+    return dict(max_abs=mabs, mean_rel=mrel)
+
+
+def check_lse_tight(real, expt, atol: float = 2e-4, rtol: float = 2e-5) -> None:
+    """LSE gate for N(0, 0.5) inputs: same -inf pattern, fp32-level agreement."""
+    real = np.asarray(real, np.float32)
+    expt = np.asarray(expt, np.float32)
+    fin = np.isfinite(expt)
+    assert np.array_equal(fin, np.isfinite(real)), "lse: -inf pattern differs"
+    assert np.array_equal(real[~fin], expt[~fin])
+    np.testing.assert_allclose(real[fin], expt[fin], rtol=rtol, atol=atol)

@@ -1,0 +1,204 @@
+"""GPU parity of the sm_100a path (``libsas.so`` through the drop-in API)
+against the reference golden's vectors and the CPU oracle.
+
+* every committed golden vector (reference scenarios with the reference's
+  own acceptance criteria; extension cases with the benchmark's bf16 gate);
+* the five benchmark workloads at full size, checked on sampled tokens
+  against the oracle (max |err| <= 2e-2, mean rel err <= 1e-3, LSE to fp32
+  precision);
+* split-KV pieces and the combine (forced worker counts), padded BSND rows,
+  empty rows, -1 / out-of-range / duplicate indices, fp16;
+* run-to-run bitwise determinism, device error word, API contract.
+"""
+
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+os.environ.setdefault("SAS_CHECK_DEVICE_ERRORS", "1")
+
+from oracle import sas_oracle as O  # noqa: E402
+from sparse_attn_sharedkv_b200 import workloads as W  # noqa: E402
+from sparse_attn_sharedkv_b200.api import sparse_attn_sharedkv  # noqa: E402
+from sparse_attn_sharedkv_b200.sparse_flash_mla_api import sparse_flash_mla  # noqa: E402
+from tests.checks import (check_lse_tight, check_north_star, check_reference_lse,  # noqa: E402
+                          check_reference_result)
+from tests.golden_cases import (attn_fixtures, case_to_numpy, fixture_case,  # noqa: E402
+                                fixture_expected)
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def run(case: W.Case, fn=sparse_attn_sharedkv, **extra):
+    c = case.to(DEV)
+    kw = c.kwargs()
+    kw.update(extra)
+    out, lse = fn(c.q, return_softmax_lse=True, **kw)
+    torch.cuda.synchronize()
+    return out.float().cpu().numpy(), lse.cpu().numpy()
+
+
+def oracle(case: W.Case, tokens=None):
+    return O.forward(**case_to_numpy(case), tokens=tokens)
+
+
+def flat_tokens(a, layout):
+    return a if layout == "TND" else a.reshape((-1,) + a.shape[2:])
+
+
+@pytest.mark.parametrize("key", sorted(attn_fixtures()))
+def test_golden_vectors(key):
+    meta = attn_fixtures()[key]
+    case = fixture_case(key)
+    out, lse = run(case)
+    exp_out, exp_lse = fixture_expected(key)
+    toks = meta["tokens"]
+    if toks is not None:
+        out, lse = out[toks], lse[toks]
+    if meta["kind"] == "reference_scenario":
+        check_reference_result(out, exp_out, meta["dtype"])
+        check_reference_lse(lse, exp_lse, meta["dtype"])
+    else:
+        check_north_star(out, exp_out)
+        check_lse_tight(lse, exp_lse)
+
+
+@pytest.mark.parametrize("cfg", range(5))
+def test_baseline_workloads_full_size(cfg):
+    case = W.baseline_case(cfg, device=DEV)
+    out, lse = run(case)
+    c = case.to("cpu")
+    T = c.q.shape[0] * (c.q.shape[1] if c.layout_q == "BSND" else 1)
+    rng = np.random.default_rng(cfg)
+    toks = sorted(set([0, T - 1] + rng.choice(T, size=min(T, 24), replace=False).tolist()))
+    o_out, o_lse = oracle(c, tokens=toks)
+    fo, fl = flat_tokens(out, c.layout_q), flat_tokens(lse, c.layout_q)
+    ro, rl = flat_tokens(o_out, c.layout_q), flat_tokens(o_lse, c.layout_q)
+    stats = check_north_star(fo[toks], ro[toks])
+    check_lse_tight(fl[toks], rl[toks])
+    print(f"cfg{cfg + 1}: {stats}")
+
+
+@pytest.mark.parametrize("num_sms", [1, 5, 37, 148, 296])
+def test_split_kv_pieces_and_combine(num_sms):
+    case = W.random_case(seed=31, layout_q="TND", H=128, q_lens=(2, 3),
+                         kv_lens=(3000, 2500), K=700, scenario=3, sinks="random")
+    out, lse = run(case, num_sms=num_sms)
+    o_out, o_lse = oracle(case)
+    check_north_star(out, o_out)
+    check_lse_tight(lse, o_lse)
+
+
+def test_split_kv_bitwise_stable_per_plan():
+    case = W.random_case(seed=32, layout_q="BSND", B=2, H=64, q_lens=(1, 1),
+                         kv_lens=(5000, 4000), K=1024, ratio=2, scenario=3)
+    a = run(case, num_sms=40)
+    b = run(case, num_sms=40)
+    assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+
+
+@pytest.mark.parametrize("kw", [
+    dict(seed=41, layout_q="TND", scenario=3, idx_mode="dirty", K=200, q_lens=(5, 3),
+         kv_lens=(900, 700)),
+    dict(seed=42, layout_q="BSND", B=2, scenario=3, q_lens=(3, 1), kv_lens=(300, 40), K=64),
+    dict(seed=43, layout_q="TND", scenario=1, q_lens=(70, 3), kv_lens=(100, 3), H=16),
+    dict(seed=44, layout_q="TND", scenario=2, ratio=8, q_lens=(6, 2), kv_lens=(1400, 600),
+         H=128),
+    dict(seed=45, layout_q="TND", scenario=3, ratio=1, win_left=-1, K=256, idx_mode="dirty",
+         q_lens=(4, 4), kv_lens=(600, 300), sinks="-inf"),
+    dict(seed=46, layout_q="TND", scenario=3, q_lens=(3, 2), kv_lens=(500, 300), K=64,
+         dtype=torch.float16),
+    dict(seed=47, layout_q="TND", scenario=1, q_lens=(3, 2), kv_lens=(2, 0), H=64,
+         sinks="random"),
+    dict(seed=48, layout_q="TND", D=512, d_v=None, scenario=3, q_lens=(4, 2),
+         kv_lens=(700, 900), K=128, H=64),
+])
+def test_edge_cases_vs_oracle(kw):
+    case = W.random_case(**kw)
+    out, lse = run(case)
+    o_out, o_lse = oracle(case)
+    check_north_star(out, o_out)
+    check_lse_tight(lse, o_lse)
+
+
+def test_empty_and_padded_rows():
+    # act_kv = 0 batch: every row has no key -> out 0, lse = sink; BSND padding -> 0 / 0.
+    case = W.random_case(seed=51, layout_q="BSND", B=2, H=64, q_lens=(3, 1),
+                         kv_lens=(50, 1), scenario=1, sinks="random")
+    out, lse = run(case)
+    o_out, o_lse = oracle(case)
+    assert np.all(out[1, 1:] == 0) and np.all(lse[1, 1:] == 0)
+    check_north_star(out, o_out)
+    check_lse_tight(lse, o_lse)
+
+
+def test_deterministic_bitwise():
+    case = W.baseline_case(2, device=DEV, scale_down=4)
+    a = run(case)
+    b = run(case)
+    assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+
+
+def test_sparse_flash_mla_entry_point_matches():
+    case = W.random_case(seed=61, layout_q="TND", scenario=3, K=128, q_lens=(4, 4),
+                         kv_lens=(800, 600))
+    a = run(case)
+    b = run(case, fn=sparse_flash_mla)
+    assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+
+
+def test_api_return_type():
+    """test_sparse_attn_sharedkv.py:608-715: both return branches."""
+    case = W.reference_scenario_case("swa_decode").to(DEV)
+    kw = case.kwargs()
+    one = sparse_attn_sharedkv(case.q, return_softmax_lse=False, **kw)
+    two = sparse_attn_sharedkv(case.q, return_softmax_lse=True, **kw)
+    assert isinstance(one, torch.Tensor)
+    assert isinstance(two, tuple) and len(two) == 2
+    out, lse = two
+    assert out.shape == (1, 64, 512) and out.dtype == torch.bfloat16
+    assert lse.shape == (1, 64) and lse.dtype == torch.float32
+    torch.testing.assert_close(out, one)
+
+
+def test_metadata_argument_accepted_and_checked():
+    case = W.reference_scenario_case("swa_decode").to(DEV)
+    kw = case.kwargs()
+    md = torch.zeros(1024, dtype=torch.int32, device=DEV)
+    sparse_attn_sharedkv(case.q, metadata=md, **kw)
+    with pytest.raises(AssertionError):
+        sparse_attn_sharedkv(case.q, metadata=md[:10], **kw)
+
+
+def test_invalid_arguments_raise():
+    case = W.reference_scenario_case("swa_decode").to(DEV)
+    kw = case.kwargs()
+    with pytest.raises(AssertionError):
+        sparse_attn_sharedkv(case.q, **dict(kw, layout_q="BNSD"))
+    with pytest.raises(AssertionError):
+        sparse_attn_sharedkv(case.q, ori_win_right=1, **kw)
+    with pytest.raises(ValueError):
+        sparse_attn_sharedkv(case.q.float(), **kw)
+
+
+def test_device_error_word_on_bad_block_table():
+    """A block id past the pool is caught by the kernel's bounds check (no
+    access, zero row) and reported through the error word."""
+    case = W.random_case(seed=71, layout_q="TND", scenario=1, q_lens=(2, 1),
+                         kv_lens=(100, 50)).to(DEV)
+    bt = case.ori_block_table.clone()
+    bt[0, 0] = case.ori_kv.shape[0] + 5
+    kw = case.kwargs()
+    kw["ori_block_table"] = bt
+    with pytest.raises(RuntimeError, match="device check failed"):
+        sparse_attn_sharedkv(case.q, **kw)
+    torch.cuda.synchronize()
+    # The context is still usable afterwards.
+    out = sparse_attn_sharedkv(case.q, **case.kwargs())
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
