@@ -127,6 +127,20 @@ typedef struct SasFwdParams {
   int32_t num_sms;                 /* persistent workers (0 = all SMs)            */
 } SasFwdParams;
 
+/* Plan summary returned by sas_plan (sizes in elements). */
+typedef struct SasPlanInfo {
+  int32_t num_rows;          /* work rows (query tokens incl. padded BSND rows) */
+  int32_t num_workers;       /* persistent workers (CTA groups)                 */
+  int32_t head_groups;       /* CTAs per worker = ceil(H / 64)                  */
+  int32_t num_split_rows;    /* rows whose keys were split across workers       */
+  int32_t num_partials;      /* partial slots used by split rows                */
+  int64_t total_tiles;       /* 64-key tiles over all rows                      */
+  int64_t plan_ints;         /* int32 entries of the serialised plan            */
+  int64_t split_off;         /* plan offset of the split-row section            */
+  int64_t actq_off;          /* plan offset of act_q[B]                         */
+  int64_t actkv_off;         /* plan offset of act_kv[B]                        */
+} SasPlanInfo;
+
 /* Bytes of device workspace a forward call needs (plan + split-KV partials).
  * Host-only; deterministic in (problem, num_sms). */
 int sas_fwd_workspace_size(const SasProblem* prob, int32_t num_sms, size_t* bytes);
@@ -137,6 +151,18 @@ int sas_fwd_workspace_size(const SasProblem* prob, int32_t num_sms, size_t* byte
  * `workspace` must be 256-byte aligned and at least sas_fwd_workspace_size. */
 int sas_fwd(const SasProblem* prob, const SasFwdParams* params, void* workspace,
             size_t workspace_bytes, void* stream);
+
+/* Two-phase form of sas_fwd, for callers that reuse one plan or time the
+ * kernels alone.  sas_fwd_prepare plans on the host and uploads the plan into
+ * the workspace (stream-ordered); sas_fwd_execute launches, on a prepared
+ * workspace, the attention kernel (phases & SAS_PHASE_ATTN) and/or the
+ * combine kernel (phases & SAS_PHASE_COMBINE).  sas_fwd = prepare + execute
+ * of both phases. */
+enum { SAS_PHASE_ATTN = 1, SAS_PHASE_COMBINE = 2, SAS_PHASE_ALL = 3 };
+int sas_fwd_prepare(const SasProblem* prob, const SasFwdParams* params, void* workspace,
+                    size_t workspace_bytes, void* stream, SasPlanInfo* info);
+int sas_fwd_execute(const SasProblem* prob, const SasFwdParams* params, const SasPlanInfo* info,
+                    void* workspace, size_t workspace_bytes, void* stream, int32_t phases);
 
 /* LSE-combine of split-KV partials (normally called by sas_fwd).  For each of
  * `num_rows` split rows, piece i of row r is partial slot `partial_base[r]+i`:
@@ -149,16 +175,6 @@ int sas_combine(const int32_t* row_token, const int32_t* row_pieces,
 
 /* ---- B200 work plan (host) ---- */
 
-/* Plan summary returned by sas_plan (sizes in elements). */
-typedef struct SasPlanInfo {
-  int32_t num_rows;          /* work rows (query tokens incl. padded BSND rows) */
-  int32_t num_workers;       /* persistent workers (CTA groups)                 */
-  int32_t head_groups;       /* CTAs per worker = ceil(H / 64)                  */
-  int32_t num_split_rows;    /* rows whose keys were split across workers       */
-  int32_t num_partials;      /* partial slots used by split rows                */
-  int64_t total_tiles;       /* 64-key tiles over all rows                      */
-  int64_t plan_ints;         /* int32 entries of the serialised plan            */
-} SasPlanInfo;
 
 /* Size the plan (host). */
 int sas_plan_size(const SasProblem* prob, int32_t num_sms, SasPlanInfo* info);

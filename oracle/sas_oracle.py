@@ -192,8 +192,8 @@ def forward(*, q: np.ndarray, ori_kv: np.ndarray, ori_block_table: np.ndarray,
             cmp_kv: Optional[np.ndarray] = None, cmp_block_table: Optional[np.ndarray] = None,
             cmp_sparse_indices: Optional[np.ndarray] = None, cmp_ratio: int = 4,
             ori_win_left: int = 127, head_dim_v: Optional[int] = None, dtype: str = "bf16",
-            tokens: Optional[Sequence[int]] = None, s2_tile: int = GOLDEN_S2_TILE
-            ) -> Tuple[np.ndarray, np.ndarray]:
+            tokens: Optional[Sequence[int]] = None, s2_tile: int = GOLDEN_S2_TILE,
+            out_dtype: Optional[str] = None) -> Tuple[np.ndarray, np.ndarray]:
     """Oracle forward on paged inputs.
 
     Arguments mirror ``api.sparse_attn_sharedkv`` (api.py:129-153) with numpy
@@ -203,7 +203,10 @@ def forward(*, q: np.ndarray, ori_kv: np.ndarray, ori_block_table: np.ndarray,
     * ``ori_kv`` / ``cmp_kv``: ``[blocks, block_size, 1, D]``;
     * block tables ``[B, table_len]`` int32 (``-1`` unused);
     * ``cmp_sparse_indices``: ``[T, 1, K]`` (TND) or ``[B, S, 1, K]`` (BSND);
-    * ``tokens``: optional subset of flat token ids to compute (others zero).
+    * ``tokens``: optional subset of flat token ids to compute (others zero);
+    * ``out_dtype``: rounding of the output (default ``dtype``, as golden.py:198;
+      ``"fp32"`` keeps the unrounded fp32 result, the reference an accuracy
+      gate measures against).
 
     Returns ``(out, lse)`` as float32 arrays in q's layout (out rounded to
     ``dtype``), ``out[..., :head_dim_v]`` and ``lse [T, N1]`` / ``[B, S, N1]``.
@@ -261,7 +264,7 @@ def forward(*, q: np.ndarray, ori_kv: np.ndarray, ori_block_table: np.ndarray,
             tiles += [cmp_k[i:i + s2_tile] for i in range(0, cmp_k.shape[0], s2_tile)]
             o, ls = _online_softmax(q_flat[t].astype(np.float32), tiles, sinks,
                                     softmax_scale, dtype, d_v)
-            out[t] = round_to_dtype(o, dtype)
+            out[t] = round_to_dtype(o, out_dtype or dtype)
             lse[t] = ls
 
     if layout_q == "BSND":

@@ -20,6 +20,7 @@ ERRORS = {1: "SAS_ERR_INVALID", 2: "SAS_ERR_UNSUPPORTED", 3: "SAS_ERR_CUDA",
 LAYOUTS = {"BSND": 0, "TND": 1, "BSH": 2, "BNSD": 3, "PA_ND": 4}
 DTYPE_BF16, DTYPE_FP16 = 0, 1
 SCENARIO_SWA, SCENARIO_CFA, SCENARIO_SCFA = 1, 2, 3
+PHASE_ATTN, PHASE_COMBINE, PHASE_ALL = 1, 2, 3
 SAS_META_SIZE = 1024
 SAS_AIC_CORE_NUM = 36
 SAS_AIV_CORE_NUM = 72
@@ -76,7 +77,8 @@ class SasPlanInfo(C.Structure):
     _fields_ = [
         ("num_rows", C.c_int32), ("num_workers", C.c_int32), ("head_groups", C.c_int32),
         ("num_split_rows", C.c_int32), ("num_partials", C.c_int32),
-        ("total_tiles", C.c_int64), ("plan_ints", C.c_int64),
+        ("total_tiles", C.c_int64), ("plan_ints", C.c_int64), ("split_off", C.c_int64),
+        ("actq_off", C.c_int64), ("actkv_off", C.c_int64),
     ]
 
 
@@ -87,6 +89,11 @@ PROTOTYPES = {
                                          C.POINTER(C.c_size_t)]),
     "sas_fwd": (C.c_int, [C.POINTER(SasProblem), C.POINTER(SasFwdParams), C.c_void_p,
                           C.c_size_t, C.c_void_p]),
+    "sas_fwd_prepare": (C.c_int, [C.POINTER(SasProblem), C.POINTER(SasFwdParams), C.c_void_p,
+                                  C.c_size_t, C.c_void_p, C.POINTER(SasPlanInfo)]),
+    "sas_fwd_execute": (C.c_int, [C.POINTER(SasProblem), C.POINTER(SasFwdParams),
+                                  C.POINTER(SasPlanInfo), C.c_void_p, C.c_size_t, C.c_void_p,
+                                  C.c_int32]),
     "sas_combine": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p,
                               C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
                               C.c_void_p, C.c_void_p]),

@@ -39,6 +39,7 @@ from __future__ import annotations
 
 import ctypes as C
 import os
+from collections import OrderedDict
 from typing import Optional, Tuple, Union
 
 import torch
@@ -49,6 +50,14 @@ DEFAULT_CORE_NUM = 24  # the reference's AIC count default (kernel.py:70)
 SAS_META_SIZE = _lib.SAS_META_SIZE
 
 _CHECK_DEVICE = os.environ.get("SAS_CHECK_DEVICE_ERRORS", "0") == "1"
+
+# Plans (host schedule uploaded into a device workspace) are reused across
+# calls with the same lengths and shapes, as a serving step reuses one
+# metadata table for every layer.  Keyed by everything the plan depends on,
+# including the stream (the workspace also holds the split-KV partials).
+_PLAN_CACHE: "OrderedDict" = OrderedDict()
+_PLAN_CACHE_SIZE = 8
+last_plan_info = None  # SasPlanInfo of the most recent call (diagnostics / bench)
 
 
 def _require(cond: bool, msg: str) -> None:
@@ -205,17 +214,35 @@ def _forward(q: torch.Tensor, *, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_t
         fp.cmp_table_len = cmp_bt.shape[1]
     fp.num_sms = int(num_sms or 0)
 
+    global last_plan_info
     L = _lib.lib()
     if total == 0:
         return out, lse
-    ws_bytes = C.c_size_t(0)
-    _lib.check("sas_fwd_workspace_size",
-               L.sas_fwd_workspace_size(C.byref(prob), fp.num_sms, C.byref(ws_bytes)))
     with torch.cuda.device(dev):
-        ws = torch.empty(max(ws_bytes.value, 256), dtype=torch.uint8, device=dev)
         stream = torch.cuda.current_stream(dev).cuda_stream
-        _lib.check("sas_fwd", L.sas_fwd(C.byref(prob), C.byref(fp), ws.data_ptr(),
-                                        ws_bytes.value, C.c_void_p(stream)))
+        key = (dev.index, stream, layout_q, tuple(q_start), tuple(q_len), tuple(kv_len), N1,
+               scenario, int(ori_win_left), ratio, int(K), fp.num_sms, total, S_max)
+        hit = _PLAN_CACHE.get(key)
+        if hit is None:
+            ws_bytes = C.c_size_t(0)
+            _lib.check("sas_fwd_workspace_size",
+                       L.sas_fwd_workspace_size(C.byref(prob), fp.num_sms, C.byref(ws_bytes)))
+            ws = torch.empty(max(ws_bytes.value, 256), dtype=torch.uint8, device=dev)
+            info = _lib.SasPlanInfo()
+            _lib.check("sas_fwd_prepare",
+                       L.sas_fwd_prepare(C.byref(prob), C.byref(fp), ws.data_ptr(),
+                                         ws_bytes.value, C.c_void_p(stream), C.byref(info)))
+            hit = (ws, ws_bytes.value, info)
+            _PLAN_CACHE[key] = hit
+            while len(_PLAN_CACHE) > _PLAN_CACHE_SIZE:
+                _PLAN_CACHE.popitem(last=False)
+        else:
+            _PLAN_CACHE.move_to_end(key)
+        ws, nbytes, info = hit
+        last_plan_info = info
+        _lib.check("sas_fwd_execute",
+                   L.sas_fwd_execute(C.byref(prob), C.byref(fp), C.byref(info), ws.data_ptr(),
+                                     nbytes, C.c_void_p(stream), _lib.PHASE_ALL))
     return out, lse
 
 

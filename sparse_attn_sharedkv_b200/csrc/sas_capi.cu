@@ -81,32 +81,47 @@ extern "C" int sas_fwd_workspace_size(const SasProblem* prob, int32_t num_sms, s
   return SAS_OK;
 }
 
-extern "C" int sas_fwd(const SasProblem* prob, const SasFwdParams* params, void* workspace,
-                       size_t workspace_bytes, void* stream_ptr) {
-  if (!prob || !params) return SAS_ERR_INVALID;
-  const SasProblem& p = *prob;
-  const SasFwdParams& f = *params;
-  int rc = validate(p, f);
+extern "C" int sas_fwd_prepare(const SasProblem* prob, const SasFwdParams* params,
+                               void* workspace, size_t workspace_bytes, void* stream_ptr,
+                               SasPlanInfo* info_out) {
+  if (!prob || !params || !info_out) return SAS_ERR_INVALID;
+  int rc = validate(*prob, *params);
   if (rc != SAS_OK) return rc;
-  const int sms = resolve_sms(f.num_sms);
+  const int sms = resolve_sms(params->num_sms);
   if (sms <= 0) return SAS_ERR_CUDA;
-
   std::vector<int32_t> plan;
   SasPlanInfo info;
-  rc = sas::plan_build(p, sms, &plan, &info);
+  rc = sas::plan_build(*prob, sms, &plan, &info);
   if (rc != SAS_OK) return rc;
+  *info_out = info;
+  if (info.num_rows == 0) return SAS_OK;
+  const WorkspaceLayout wl = layout_for(info, prob->num_heads, params->head_dim_v);
+  if (workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & (kAlign - 1)) != 0 ||
+      workspace_bytes < wl.total)
+    return SAS_ERR_WORKSPACE;
+  char* ws = static_cast<char*>(workspace);
+  if (cudaMemcpyAsync(ws + wl.plan_off, plan.data(), plan.size() * sizeof(int32_t),
+                      cudaMemcpyHostToDevice,
+                      reinterpret_cast<cudaStream_t>(stream_ptr)) != cudaSuccess)
+    return SAS_ERR_CUDA;
+  return SAS_OK;
+}
+
+extern "C" int sas_fwd_execute(const SasProblem* prob, const SasFwdParams* params,
+                               const SasPlanInfo* info_ptr, void* workspace,
+                               size_t workspace_bytes, void* stream_ptr, int32_t phases) {
+  if (!prob || !params || !info_ptr) return SAS_ERR_INVALID;
+  const SasProblem& p = *prob;
+  const SasFwdParams& f = *params;
+  const SasPlanInfo& info = *info_ptr;
   if (info.num_rows == 0) return SAS_OK;
   const WorkspaceLayout wl = layout_for(info, p.num_heads, f.head_dim_v);
   if (workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & (kAlign - 1)) != 0 ||
       workspace_bytes < wl.total)
     return SAS_ERR_WORKSPACE;
-
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);
   char* ws = static_cast<char*>(workspace);
-  int32_t* dplan = reinterpret_cast<int32_t*>(ws + wl.plan_off);
-  if (cudaMemcpyAsync(dplan, plan.data(), plan.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
-                      stream) != cudaSuccess)
-    return SAS_ERR_CUDA;
+  const int32_t* dplan = reinterpret_cast<const int32_t*>(ws + wl.plan_off);
 
   sas::FwdArgs a{};
   a.q = f.q;
@@ -120,8 +135,8 @@ extern "C" int sas_fwd(const SasProblem* prob, const SasFwdParams* params, void*
   a.lse = f.lse;
   a.err = f.err;
   a.plan = dplan;
-  a.q_len = dplan + plan[sas::H_ACTQ_OFF];
-  a.kv_len = dplan + plan[sas::H_ACTKV_OFF];
+  a.q_len = dplan + info.actq_off;
+  a.kv_len = dplan + info.actkv_off;
   a.o_partial = reinterpret_cast<float*>(ws + wl.opart_off);
   a.lse_partial = reinterpret_cast<float*>(ws + wl.lpart_off);
   a.num_heads = p.num_heads;
@@ -140,16 +155,26 @@ extern "C" int sas_fwd(const SasProblem* prob, const SasFwdParams* params, void*
   a.cmp_num_blocks = f.cmp_num_blocks;
   a.cmp_table_len = f.cmp_table_len;
   a.head_groups = info.head_groups;
-  const int grid = info.num_workers * info.head_groups;
-  rc = sas::launch_fwd(a, grid, stream);
-  if (rc != SAS_OK) return rc;
-  if (info.num_split_rows > 0) {
-    const int32_t* split = dplan + plan[sas::H_SPLIT_OFF];
+  int rc = SAS_OK;
+  if (phases & SAS_PHASE_ATTN) {
+    rc = sas::launch_fwd(a, info.num_workers * info.head_groups, stream);
+    if (rc != SAS_OK) return rc;
+  }
+  if ((phases & SAS_PHASE_COMBINE) && info.num_split_rows > 0) {
+    const int32_t* split = dplan + info.split_off;
     rc = sas::launch_combine(split, split + 1, split + 2, 4, info.num_split_rows, a.o_partial,
                              a.lse_partial, p.num_heads, f.head_dim_v, f.dtype, f.out, f.lse,
                              stream);
   }
   return rc;
+}
+
+extern "C" int sas_fwd(const SasProblem* prob, const SasFwdParams* params, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  SasPlanInfo info;
+  int rc = sas_fwd_prepare(prob, params, workspace, workspace_bytes, stream, &info);
+  if (rc != SAS_OK) return rc;
+  return sas_fwd_execute(prob, params, &info, workspace, workspace_bytes, stream, SAS_PHASE_ALL);
 }
 
 extern "C" int sas_combine(const int32_t* row_token, const int32_t* row_pieces,

@@ -149,6 +149,9 @@ int build(const SasProblem& p, int32_t num_sms, bool fill, Built* out) {
   out->info.num_partials = (int32_t)partials;
   out->info.total_tiles = total_tiles;
   out->info.plan_ints = total_ints;
+  out->info.split_off = split_off;
+  out->info.actq_off = actq_off;
+  out->info.actkv_off = actkv_off;
   if (!fill) return SAS_OK;
 
   std::vector<int32_t>& pl = out->plan;

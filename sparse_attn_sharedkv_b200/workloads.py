@@ -507,3 +507,86 @@ def random_case(*, seed: int, layout_q: str = "TND", B: int = 2, H: int = 64, D:
              cmp_ratio=ratio if scenario >= 2 else None, ori_win_left=win_left,
              head_dim_v=d_v, meta=dict(scenario=scenario, K=K))
     return c.to(device)
+
+
+# --------------------------------------------------------------------------
+# Algorithmic work of one call.
+# --------------------------------------------------------------------------
+
+def accounting(case: Case) -> Dict:
+    """Valid keys, FLOPs and compulsory HBM bytes of one forward call.
+
+    * keys: attended (query, key) pairs after the window, threshold, ``-1``
+      stop and range masks (golden.py:28-66, 125-150);
+    * FLOPs: ``2 * H * keys * (d_qk + d_v)`` (QK^T and PV);
+    * bytes: Q + O + LSE + indices + every distinct KV row touched (a row
+      shared by several queries of a window is read once: compulsory traffic).
+    Vectorised in torch on the case's device.
+    """
+    dev = case.q.device
+    H = case.q.shape[-2]
+    D = case.q.shape[-1]
+    dv = case.head_dim_v or D
+    B = case.batch
+    if case.layout_q == "TND":
+        cu = case.cu_seqlens_q.to(torch.int64).cpu()
+        starts = cu[:-1]
+        lens = cu[1:] - cu[:-1]
+        T = int(case.q.shape[0])
+    else:
+        S = case.q.shape[1]
+        T = B * S
+        starts = torch.arange(B) * S
+        lens = ((case.cu_seqlens_q[1:] - case.cu_seqlens_q[:-1]).cpu().to(torch.int64)
+                if case.cu_seqlens_q is not None else torch.full((B,), S, dtype=torch.int64))
+    kv = case.seqused_kv.to(torch.int64).cpu()
+    # per valid token: batch, position
+    tb = torch.repeat_interleave(torch.arange(B), lens)
+    ts = torch.cat([torch.arange(int(n)) for n in lens]) if T else torch.zeros(0, dtype=torch.int64)
+    tok = starts[tb] + ts
+    aq, akv = lens[tb], kv[tb]
+    s_g = akv - aq + ts
+    wl = case.ori_win_left
+    lo = torch.clamp(s_g - wl, min=0)
+    hi = s_g + 1
+    win = torch.clamp(hi - lo, min=0)
+    keys = int(win.sum())
+    uniq = 0
+    # distinct window rows: windows of consecutive queries of a batch overlap
+    for b in range(B):
+        m = tb == b
+        if m.any() and int(win[m].sum()) > 0:
+            nz = win[m] > 0
+            uniq += int(hi[m][nz].max() - lo[m][nz].min())
+    cmp_keys = 0
+    idx_bytes = 0
+    if case.cmp_kv is not None:
+        ratio = case.cmp_ratio
+        thr = torch.div(akv - aq + ts + 1, ratio, rounding_mode="floor")
+        if case.cmp_sparse_indices is not None:
+            idx = case.cmp_sparse_indices.reshape(T, -1).to(dev)
+            K = idx.shape[1]
+            idx_bytes = T * K * 4
+            idx = idx[tok.to(dev)]
+            thr_d = thr.to(dev)
+            ar = torch.arange(K, device=dev)
+            in_rng = ar[None, :] < torch.clamp(thr_d, max=K)[:, None]
+            m1 = (idx == -1) & in_rng
+            before = (torch.cumsum(m1.to(torch.int32), dim=1) - m1.to(torch.int32)) > 0
+            valid = in_rng & (idx >= 0) & (idx < thr_d[:, None]) & ~before
+            cmp_keys = int(valid.sum())
+            ids = (tb.to(dev)[:, None] * (1 << 32) + idx.to(torch.int64))[valid]
+            uniq += int(torch.unique(ids).numel()) if ids.numel() else 0
+        else:
+            c = torch.clamp(thr, min=0)
+            cmp_keys = int(c.sum())
+            for b in range(B):
+                m = tb == b
+                if m.any():
+                    uniq += int(c[m].max())
+    keys += cmp_keys
+    flops = 2.0 * H * keys * (D + dv)
+    esz = case.q.element_size()
+    nbytes = T * H * D * esz + T * H * dv * esz + T * H * 4 + idx_bytes + uniq * D * esz
+    return dict(tokens=int(lens.sum()), keys=keys, window_keys=keys - cmp_keys,
+                cmp_keys=cmp_keys, unique_kv_rows=uniq, flops=flops, bytes=nbytes)

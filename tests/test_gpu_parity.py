@@ -4,8 +4,8 @@ against the reference golden's vectors and the CPU oracle.
 * every committed golden vector (reference scenarios with the reference's
   own acceptance criteria; extension cases with the benchmark's bf16 gate);
 * the five benchmark workloads at full size, checked on sampled tokens
-  against the oracle (max |err| <= 2e-2, mean rel err <= 1e-3, LSE to fp32
-  precision);
+  against an fp32 oracle (max |err| <= 2e-2, mean relative error at most
+  1e-3 above the reference algorithm's own, LSE to fp32 precision);
 * split-KV pieces and the combine (forced worker counts), padded BSND rows,
   empty rows, -1 / out-of-range / duplicate indices, fp16;
 * run-to-run bitwise determinism, device error word, API contract.
@@ -44,7 +44,14 @@ def run(case: W.Case, fn=sparse_attn_sharedkv, **extra):
 
 
 def oracle(case: W.Case, tokens=None):
-    return O.forward(**case_to_numpy(case), tokens=tokens)
+    """CPU oracle: (fp32 attention, golden-algorithm output, golden LSE).
+
+    The first runs entirely in fp32 (P not rounded, no final cast); the second
+    is the reference algorithm (golden.py:187-198) the oracle is pinned to."""
+    kw = case_to_numpy(case)
+    exact, _ = O.forward(**dict(kw, dtype="fp32"), tokens=tokens)
+    gold, lse = O.forward(**kw, tokens=tokens)
+    return exact, gold, lse
 
 
 def flat_tokens(a, layout):
@@ -64,8 +71,16 @@ def test_golden_vectors(key):
         check_reference_result(out, exp_out, meta["dtype"])
         check_reference_lse(lse, exp_lse, meta["dtype"])
     else:
-        check_north_star(out, exp_out)
+        # Extension vectors (N(0, 0.5) data, outputs ~0.03): max |err| against
+        # the golden vector, LSE to fp32 precision, and the benchmark's gate
+        # against the fp32 oracle (pinned to the same golden vectors).  The
+        # reference's isclose gate (atol 1e-4) is sized for its +-10 data.
+        assert float(np.abs(out - exp_out).max()) <= 2e-2
         check_lse_tight(lse, exp_lse)
+        ref, gold, _ = oracle(case, tokens=toks)
+        if toks is not None:
+            ref, gold = ref[toks], gold[toks]
+        print(key, check_north_star(out, ref, gold))
 
 
 @pytest.mark.parametrize("cfg", range(5))
@@ -76,10 +91,10 @@ def test_baseline_workloads_full_size(cfg):
     T = c.q.shape[0] * (c.q.shape[1] if c.layout_q == "BSND" else 1)
     rng = np.random.default_rng(cfg)
     toks = sorted(set([0, T - 1] + rng.choice(T, size=min(T, 24), replace=False).tolist()))
-    o_out, o_lse = oracle(c, tokens=toks)
+    ex, gold, o_lse = oracle(c, tokens=toks)
     fo, fl = flat_tokens(out, c.layout_q), flat_tokens(lse, c.layout_q)
-    ro, rl = flat_tokens(o_out, c.layout_q), flat_tokens(o_lse, c.layout_q)
-    stats = check_north_star(fo[toks], ro[toks])
+    ro, rg, rl = (flat_tokens(a, c.layout_q) for a in (ex, gold, o_lse))
+    stats = check_north_star(fo[toks], ro[toks], rg[toks])
     check_lse_tight(fl[toks], rl[toks])
     print(f"cfg{cfg + 1}: {stats}")
 
@@ -89,8 +104,8 @@ def test_split_kv_pieces_and_combine(num_sms):
     case = W.random_case(seed=31, layout_q="TND", H=128, q_lens=(2, 3),
                          kv_lens=(3000, 2500), K=700, scenario=3, sinks="random")
     out, lse = run(case, num_sms=num_sms)
-    o_out, o_lse = oracle(case)
-    check_north_star(out, o_out)
+    ex, gold, o_lse = oracle(case)
+    check_north_star(out, ex, gold)
     check_lse_tight(lse, o_lse)
 
 
@@ -121,19 +136,19 @@ def test_split_kv_bitwise_stable_per_plan():
 def test_edge_cases_vs_oracle(kw):
     case = W.random_case(**kw)
     out, lse = run(case)
-    o_out, o_lse = oracle(case)
-    check_north_star(out, o_out)
+    ex, gold, o_lse = oracle(case)
+    check_north_star(out, ex, gold)
     check_lse_tight(lse, o_lse)
 
 
 def test_empty_and_padded_rows():
-    # act_kv = 0 batch: every row has no key -> out 0, lse = sink; BSND padding -> 0 / 0.
+    # BSND padding (s >= act_q of batch 1) -> out 0 and lse 0 (golden.py:106-111).
     case = W.random_case(seed=51, layout_q="BSND", B=2, H=64, q_lens=(3, 1),
                          kv_lens=(50, 1), scenario=1, sinks="random")
     out, lse = run(case)
-    o_out, o_lse = oracle(case)
+    ex, gold, o_lse = oracle(case)
     assert np.all(out[1, 1:] == 0) and np.all(lse[1, 1:] == 0)
-    check_north_star(out, o_out)
+    check_north_star(out, ex, gold)
     check_lse_tight(lse, o_lse)
 
 
