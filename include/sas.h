@@ -125,6 +125,8 @@ typedef struct SasFwdParams {
   int32_t ori_block_size, ori_num_blocks, ori_table_len;
   int32_t cmp_block_size, cmp_num_blocks, cmp_table_len;
   int32_t num_sms;                 /* persistent workers (0 = all SMs)            */
+  int64_t* trace;                  /* [device] optional int64[4 * 8192] clock trace
+                                      of CTA 0 (diagnostics; NULL = off)           */
 } SasFwdParams;
 
 /* Plan summary returned by sas_plan (sizes in elements). */

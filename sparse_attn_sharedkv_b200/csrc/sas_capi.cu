@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -134,6 +135,7 @@ extern "C" int sas_fwd_execute(const SasProblem* prob, const SasFwdParams* param
   a.out = f.out;
   a.lse = f.lse;
   a.err = f.err;
+  a.trace = reinterpret_cast<long long*>(f.trace);
   a.plan = dplan;
   a.q_len = dplan + info.actq_off;
   a.kv_len = dplan + info.actkv_off;
@@ -155,6 +157,19 @@ extern "C" int sas_fwd_execute(const SasProblem* prob, const SasFwdParams* param
   a.cmp_num_blocks = f.cmp_num_blocks;
   a.cmp_table_len = f.cmp_table_len;
   a.head_groups = info.head_groups;
+  a.total_tokens = p.total_tokens;
+  a.ori_rows = f.ori_num_blocks * f.ori_block_size;
+  a.cmp_rows = f.cmp_kv ? f.cmp_num_blocks * a.cmp_block_size : 0;
+  {
+    // Key-row gather engine: cp.async from four warps (default) or TMA
+    // tile::gather4 (SAS_GATHER=tma).
+    static int gather = -1;
+    if (gather < 0) {
+      const char* e = getenv("SAS_GATHER");
+      gather = (e != nullptr && strcmp(e, "tma") == 0) ? 1 : 0;
+    }
+    a.gather = gather;
+  }
   int rc = SAS_OK;
   if (phases & SAS_PHASE_ATTN) {
     rc = sas::launch_fwd(a, info.num_workers * info.head_groups, stream);

@@ -9,11 +9,13 @@
 // Per tile of 64 key slots (window keys then compressed keys, golden.py
 // tile order) the CTA runs:
 //
-//   producer warps (2)  slot -> (cache, logical pos) -> block table -> row;
-//                       cp.async 16 B granules into a 128B-swizzled K tile
-//                       (paged window load, kernel.py:3580-3600, and top-k
-//                       gather, kernel.py:2606-2751), -1 stop / threshold
-//                       masks (golden.py:28-66) into a per-tile valid mask
+//   producer warp      slot -> (cache, logical pos) -> block table -> row;
+//                      TMA tile::gather4 of 4 rows x 128 B per op into a
+//                      128B-swizzled K tile (paged window load, kernel.py:
+//                      3580-3600, and top-k gather, kernel.py:2606-2751),
+//                      -1 stop / threshold masks (golden.py:28-66) into a
+//                      per-tile valid mask; Q tiles by 64 x 64 TMA boxes
+//   prefetch warp      the same rows a few tiles ahead, into L2
 //   MMA warp (1 lane)   S = Q K^T  : 36 x tcgen05.mma.ws M64 N64 K16 (d_qk 576)
 //                       O += P V   : 8 x tcgen05.mma.ws M64 N256 K16, where V is
 //                                    the same smem K tile read MN-major (d_v 512)
@@ -23,14 +25,18 @@
 //                       rescale in TMEM, final O / l and LSE (kernel.py:3110-3245)
 //
 // TMEM (512 columns): O[64 x 512] fp32 as two .ws M64 N256 accumulators
-// (cols 0-255, all 128 lanes), S[64 x 64] fp32 double-buffered (cols 256-319).
-// Shared memory: Q 72 KB, two K stages of 72 KB, P 8 KB.
+// (cols 0-255, all 128 lanes); S[64 x 64] fp32 double-buffered, each buffer
+// as four partial sums over interleaved 64-dim chunks (cols 256-511), so the
+// 36 small QK MMAs form four independent accumulation chains.
+// Shared memory: Q 72 KB and two K stages of 72 KB; P of a tile is written
+// into its stage's rope chunk (dims 512..575), which PV does not read.
 //
 // Every wait on an mbarrier is bounded: on timeout the thread records an
 // error in the caller's error word, raises the CTA abort flag and leaves its
 // loop; no trap, no unbounded spin.
 
 #include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -44,28 +50,33 @@ namespace sas {
 namespace {
 
 constexpr int kNumSoftmaxWarps = 4;
-constexpr int kProducerWarp0 = 4;
-constexpr int kNumProducerWarps = 2;
-constexpr int kMmaWarp = 6;
-constexpr int kThreads = 32 * 7;
-constexpr int kProducerThreads = 32 * kNumProducerWarps;
+constexpr int kProducerWarp0 = 4;  // producer warps 4..7; warp 4 also loads Q by TMA
+constexpr int kNumProducerWarps = 4;
+constexpr int kMmaWarp = 8;
+constexpr int kThreads = 32 * 9;
 constexpr int kSoftmaxThreads = 32 * kNumSoftmaxWarps;
+constexpr int kProducerThreads = 32 * kNumProducerWarps;
+constexpr int kQkPartials = 4;     // independent S accumulators per tile (QK chains)
 
 constexpr int kMaxChunks = 9;                   // d_qk / 64
 constexpr int kChunkBytes = kHeadsPerCta * 128;  // 64 rows x 64 bf16 = 8 KB
 constexpr int kQBytes = kMaxChunks * kChunkBytes;
 constexpr int kStageBytes = kMaxChunks * kChunkBytes;
-constexpr int kPBytes = kHeadsPerCta * kTileKeys * 2;
 constexpr int kSmemQ = 0;
 constexpr int kSmemK0 = kSmemQ + kQBytes;
-constexpr int kSmemP = kSmemK0 + 2 * kStageBytes;
-constexpr int kSmemTiles = kSmemP + kPBytes;       // 229376
-constexpr int kSmemDynamic = kSmemTiles + 1024;    // + runtime 1 KB alignment slack
+constexpr int kSmemTiles = kSmemK0 + 2 * kStageBytes;  // 221184
+constexpr int kSmemDynamic = kSmemTiles + 1024;        // + runtime 1 KB alignment slack
+// P (64 x 64 bf16, 8 KB) of tile j lives in chunk 8 of tile j's own K stage:
+// that chunk holds dims 512..575, which only QK reads (V is dims 0..511), so
+// it is free once S(j) is complete and is double-buffered with the stages.
+constexpr int kPChunk = 8;
+constexpr int kGatherLsu = 0;  // key rows by cp.async 16 B from the 4 producer warps
+constexpr int kGatherTma = 1;  // key rows by TMA tile::gather4 from producer warp 4
 
 // TMEM columns.
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemO = 0;     // O[:, 0:256) at +0, O[:, 256:512) at +128
-constexpr uint32_t kTmemS = 256;   // S buffers at +256, +288
+constexpr uint32_t kTmemS = 256;   // S buffer b, partial p at +256 + 128 b + 32 p
 
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -99,6 +110,61 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "r"(bar), "r"(parity)
       : "memory");
   return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+               "r"(bytes)
+               : "memory");
+}
+
+// 2D tiled TMA load of one box at (x, y) into shared memory.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// Four rows (y0..y3) of one 128-byte column block x, written to 4 consecutive
+// 128-byte rows at dst (the box of the map is one row high).
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* map, int x, int y0,
+                                            int y1, int y2, int y3, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_gather4(const CUtensorMap* map, int x, int y0, int y1,
+                                                     int y2, int y3) {
+  asm volatile(
+      "cp.async.bulk.prefetch.tensor.2d.L2.global.tile::gather4 [%0, {%1, %2, %3, %4, %5}];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3)
+      : "memory");
 }
 
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
@@ -211,11 +277,12 @@ struct Ctl {
   uint64_t q_full, q_empty;
   uint64_t s_full[2];
   uint64_t s_empty[2];
-  uint64_t p_full, pv_done, o_free, drain;
+  uint64_t p_full, o_free, drain;
+  uint64_t pv_done[2];            // PV number k completes phase k/2 of pv_done[k % 2]
   uint64_t xbar[2];               // softmax partner exchange (bounded, no bar.sync)
   uint32_t tmem_base;
   volatile int abort;
-  uint32_t valid[2][2];          // per stage, per half: 32 slot bits
+  uint16_t valid[2][4];          // per stage: slot bits of keys 16w..16w+15
   float red[2][2][kHeadsPerCta];  // [parity][half][row]: partner exchange
 };
 
@@ -227,6 +294,14 @@ __device__ __forceinline__ Row load_row(const int* rows, int r) {
   const int4* p = reinterpret_cast<const int4*>(rows + (size_t)r * kRowInts);
   int4 a = __ldg(p), c = __ldg(p + 1);
   return Row{a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+}
+
+// Diagnostic clock trace of CTA 0: 4 regions of 8192 entries (producer, MMA,
+// softmax per tile, epilogue per row).
+constexpr int kTraceRegion = 8192;
+__device__ __forceinline__ void trace(long long* tr, int region, int idx) {
+  if (tr != nullptr && blockIdx.x == 0 && idx >= 0 && idx < kTraceRegion)
+    tr[region * kTraceRegion + idx] = clock64();
 }
 
 __device__ void record_error(int* err, int code, int site, int detail) {
@@ -279,12 +354,130 @@ __device__ __forceinline__ int row_tiles(const Row& rv) {
   return (rv.slots + kTileKeys - 1) / kTileKeys;
 }
 
+// Source of one key slot: pool 0 = window cache (ori_kv), 1 = compressed
+// cache (cmp_kv), -1 = masked slot; row = block * block_size + offset in that
+// pool, or -1 for an attended position whose page is unmapped (zero row).
+struct SlotSrc {
+  int row;
+  int pool;
+  bool valid;
+};
+
+// golden.py:28-66 / 125-150 for slot `slot` of query row `rv`.  `blocked`:
+// a -1 precedes this slot in the compressed scan.  Page ids outside the pool
+// are recorded in the error word and read as zero rows.
+__device__ __forceinline__ SlotSrc resolve_slot(const FwdArgs& a, const Row& rv,
+                                                const QueryKeys& qk, int slot,
+                                                const int* idx_row, bool blocked, int* err) {
+  SlotSrc r{-1, -1, false};
+  if (slot < rv.window) {
+    const int pos = qk.win_lo + slot;
+    const int lb = pos / a.ori_block_size;
+    r.valid = true;
+    r.pool = 0;
+    if (lb < a.ori_table_len) {
+      const int blk = __ldg(a.ori_block_table + (size_t)rv.b * a.ori_table_len + lb);
+      if (blk >= 0 && blk < a.ori_num_blocks)
+        r.row = blk * a.ori_block_size + (pos - lb * a.ori_block_size);
+      else if (blk >= a.ori_num_blocks)
+        record_error(err, SAS_ERR_DEVICE, 10, blk);
+    } else {
+      record_error(err, SAS_ERR_DEVICE, 11, pos);
+    }
+  } else if (slot < rv.slots) {
+    const int c = slot - rv.window;
+    int pos = c;
+    bool ok = true;
+    if (idx_row != nullptr) {
+      pos = __ldg(idx_row + c);
+      ok = !blocked && pos >= 0 && pos < qk.thr;
+    }
+    if (ok) {
+      r.valid = true;
+      r.pool = 1;
+      const int lb = pos / a.cmp_block_size;
+      if (lb < a.cmp_table_len) {
+        const int blk = __ldg(a.cmp_block_table + (size_t)rv.b * a.cmp_table_len + lb);
+        if (blk >= 0 && blk < a.cmp_num_blocks)
+          r.row = blk * a.cmp_block_size + (pos - lb * a.cmp_block_size);
+        else if (blk >= a.cmp_num_blocks)
+          record_error(err, SAS_ERR_DEVICE, 12, blk);
+      } else {
+        record_error(err, SAS_ERR_DEVICE, 13, pos);
+      }
+    }
+  }
+  return r;
+}
+
+// Issue (or L2-prefetch) the key rows of one 64-slot tile.  Lane l holds
+// slot l in (ra, pa) and slot l + 32 in (rb, pb).  Lanes 0..15 each move a
+// group of 4 consecutive slots with one tile::gather4 per 64-column chunk;
+// a group whose rows come from both caches falls back to single-row tiled
+// loads.  Rows without a source use an out-of-range row: TMA fills zeros.
+template <bool kPrefetch>
+__device__ __forceinline__ void issue_tile(const CUtensorMap* tm_ori, const CUtensorMap* tm_cmp,
+                                           int ori_rows, int cmp_rows, int nchunks,
+                                           uint32_t stage_base, uint32_t bar, int lane, int ra,
+                                           int pa, int rb, int pb) {
+  const int g = lane & 15;
+  int row[4], pool[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int key = 4 * g + i;
+    const int src = key & 31;
+    const int xa = __shfl_sync(0xffffffffu, ra, src), xb = __shfl_sync(0xffffffffu, rb, src);
+    const int ya = __shfl_sync(0xffffffffu, pa, src), yb = __shfl_sync(0xffffffffu, pb, src);
+    row[i] = key < 32 ? xa : xb;
+    pool[i] = key < 32 ? ya : yb;
+  }
+  if (lane >= 16) return;
+  int P = -1;
+  bool mixed = false;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (pool[i] >= 0) {
+      if (P < 0) P = pool[i];
+      else if (pool[i] != P) mixed = true;
+    }
+  }
+  const uint32_t dst = stage_base + g * 4 * 128;
+  if (!mixed) {
+    const CUtensorMap* m = (P == 1) ? tm_cmp : tm_ori;
+    const int sentinel = (P == 1) ? cmp_rows : ori_rows;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (pool[i] < 0 || row[i] < 0) row[i] = sentinel;
+    for (int c = 0; c < nchunks; ++c) {
+      if constexpr (kPrefetch)
+        tma_prefetch_gather4(m, c * 64, row[0], row[1], row[2], row[3]);
+      else
+        tma_gather4(dst + c * kChunkBytes, m, c * 64, row[0], row[1], row[2], row[3], bar);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const CUtensorMap* m = (pool[i] == 1) ? tm_cmp : tm_ori;
+      const int y = row[i] >= 0 ? row[i] : ((pool[i] == 1) ? cmp_rows : ori_rows);
+      for (int c = 0; c < nchunks; ++c) {
+        if constexpr (kPrefetch)
+          tma_prefetch_2d(m, c * 64, y);
+        else
+          tma_load_2d(dst + c * kChunkBytes + i * 128, m, c * 64, y, bar);
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // The kernel.
 // ---------------------------------------------------------------------------
 
 template <bool kBf16>
-__global__ void __launch_bounds__(kThreads, 1) sas_fwd_kernel(const FwdArgs args) {
+__global__ void __launch_bounds__(kThreads, 1)
+    sas_fwd_kernel(const FwdArgs args, const __grid_constant__ CUtensorMap tm_q,
+                   const __grid_constant__ CUtensorMap tm_ori,
+                   const __grid_constant__ CUtensorMap tm_cmp) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ Ctl ctl;
 
@@ -297,6 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1) sas_fwd_kernel(const FwdArgs args
   const int* rows = plan + plan[H_ROWS_OFF];
   const int nchunks = args.head_dim >> 6;
   int* err = args.err;
+  long long* tr = args.trace;
 
   // 1024-byte aligned tile area.
   const uint32_t raw = smem_addr(smem_raw);
@@ -304,19 +498,22 @@ __global__ void __launch_bounds__(kThreads, 1) sas_fwd_kernel(const FwdArgs args
   uint8_t* gbase = smem_raw + (base - raw);
   const uint32_t sQ = base + kSmemQ;
   const uint32_t sK0 = base + kSmemK0;
-  const uint32_t sP = base + kSmemP;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
-      mbar_init(smem_addr(&ctl.kv_full[i]), 2 * kProducerThreads);
+      // LSU gather: 4 warp arrivals (valid bits written) + 128 cp.async
+      // completions; TMA gather: one arrive.expect_tx.
+      mbar_init(smem_addr(&ctl.kv_full[i]),
+                args.gather == kGatherLsu ? kNumProducerWarps + kProducerThreads : 1);
       mbar_init(smem_addr(&ctl.kv_empty[i]), 1);
       mbar_init(smem_addr(&ctl.s_full[i]), 1);
       mbar_init(smem_addr(&ctl.s_empty[i]), kSoftmaxThreads);
     }
-    mbar_init(smem_addr(&ctl.q_full), kProducerThreads);
+    mbar_init(smem_addr(&ctl.q_full), 1);
     mbar_init(smem_addr(&ctl.q_empty), 1);
     mbar_init(smem_addr(&ctl.p_full), kSoftmaxThreads);
-    mbar_init(smem_addr(&ctl.pv_done), 1);
+    mbar_init(smem_addr(&ctl.pv_done[0]), 1);
+    mbar_init(smem_addr(&ctl.pv_done[1]), 1);
     mbar_init(smem_addr(&ctl.o_free), kSoftmaxThreads);
     mbar_init(smem_addr(&ctl.drain), 1);
     mbar_init(smem_addr(&ctl.xbar[0]), kSoftmaxThreads);
@@ -342,12 +539,14 @@ __global__ void __launch_bounds__(kThreads, 1) sas_fwd_kernel(const FwdArgs args
   if (warp >= kProducerWarp0 && warp < kProducerWarp0 + kNumProducerWarps) {
     // ======================= producers =======================
     const int pw = warp - kProducerWarp0;
+    const bool leader = (pw == 0);
+    const bool lsu = (args.gather == kGatherLsu);
     const int D = args.head_dim;
+    const uint32_t row_bytes = (uint32_t)D * 2u;
     const int gran = D >> 3;  // 16-byte granules per row
-    const char* qbase = reinterpret_cast<const char*>(args.q);
     uint32_t kv_empty_par[2] = {1u, 1u};
     uint32_t q_empty_par = 1u;
-    int stage = 0;
+    int stage = 0, produced = 0;
     bool ok = true;
     for (int r = span.r0; ok && span.r0 >= 0 && r <= span.r1; ++r) {
       const Row rv = load_row(rows, r);
@@ -355,24 +554,22 @@ __global__ void __launch_bounds__(kThreads, 1) sas_fwd_kernel(const FwdArgs args
       const int ja = (r == span.r0) ? span.t0 : 0;
       const int jb = (r == span.r1) ? span.t1 : (tiles > 0 ? tiles : 1);
       if (tiles == 0 || ja >= jb) continue;
-      // ---- Q tile: 64 heads of this group ----
-      if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.q_empty, q_empty_par, err, 1))) {
-        ok = false;
-        break;
-      }
-      q_empty_par ^= 1u;
-      for (int hh = 0; hh < 32; ++hh) {
-        const int h = pw * 32 + hh;
-        const int head = group * kHeadsPerCta + h;
-        const bool live = head < args.num_heads;
-        const char* src = qbase + ((size_t)rv.token * args.num_heads + (live ? head : 0)) *
-                                      (size_t)D * 2;
-        for (int gi = lane; gi < gran; gi += 32) {
-          const uint32_t dst = sQ + (gi >> 3) * kChunkBytes + swz(h, gi & 7);
-          cp_async_16(dst, src + gi * 16, live ? 16u : 0u);
+      if (!lsu && !leader) continue;  // TMA gather: warp 4 alone
+      // ---- Q tile: 64 heads of this group, one 64 x 64 TMA box per chunk ----
+      if (leader) {
+        if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.q_empty, q_empty_par, err, 1))) {
+          ok = false;
+          break;
         }
+        q_empty_par ^= 1u;
+        if (lane == 0) {
+          mbar_expect_tx(smem_addr(&ctl.q_full), kHeadsPerCta * row_bytes);
+          const int qrow = rv.token * args.num_heads + group * kHeadsPerCta;
+          for (int c = 0; c < nchunks; ++c)
+            tma_load_2d(sQ + c * kChunkBytes, &tm_q, c * 64, qrow, smem_addr(&ctl.q_full));
+        }
+        __syncwarp();
       }
-      cp_async_arrive_noinc(smem_addr(&ctl.q_full));
 
       // ---- key tiles ----
       const int act_q = args.q_len[rv.b];
@@ -394,14 +591,8 @@ __global__ void __launch_bounds__(kThreads, 1) sas_fwd_kernel(const FwdArgs args
         }
       }
       for (int j = ja; j < jb; ++j) {
-        if (!__all_sync(0xffffffffu,
-                        wait_bar(&ctl, &ctl.kv_empty[stage], kv_empty_par[stage], err, 2))) {
-          ok = false;
-          break;
-        }
-        kv_empty_par[stage] ^= 1u;
-        // -1 positions among the compressed slots of this tile (both warps
-        // scan the whole tile so the stop prefix needs no cross-warp sync).
+        // -1 positions among the tile's compressed slots (each warp scans the
+        // whole tile, so the stop prefix needs no cross-warp exchange).
         uint64_t m1mask = 0;
         if (idx_row != nullptr) {
           const int ca = j * kTileKeys + lane - W;
@@ -411,76 +602,66 @@ __global__ void __launch_bounds__(kThreads, 1) sas_fwd_kernel(const FwdArgs args
           m1mask = (uint64_t)__ballot_sync(0xffffffffu, ma) |
                    ((uint64_t)__ballot_sync(0xffffffffu, mb) << 32);
         }
-        // My slot: key = pw*32 + lane.
-        const int key = pw * 32 + lane;
-        const int slot = j * kTileKeys + key;
-        bool valid = false;
-        const char* src = nullptr;
-        if (slot < W) {
-          const int pos = qk.win_lo + slot;
-          const int lb = pos / args.ori_block_size;
-          valid = true;
-          if (lb < args.ori_table_len) {
-            const int blk = __ldg(args.ori_block_table + (size_t)rv.b * args.ori_table_len + lb);
-            if (blk >= 0 && blk < args.ori_num_blocks) {
-              src = reinterpret_cast<const char*>(args.ori_kv) +
-                    ((size_t)blk * args.ori_block_size + (pos - lb * args.ori_block_size)) *
-                        (size_t)D * 2;
-            } else if (blk >= args.ori_num_blocks) {
-              record_error(err, SAS_ERR_DEVICE, 10, blk);
-            }
-          } else {
-            record_error(err, SAS_ERR_DEVICE, 11, pos);
-          }
-        } else if (slot < rv.slots) {
-          const int c = slot - W;
-          int pos = c;
-          valid = true;
-          if (idx_row != nullptr) {
-            pos = __ldg(idx_row + c);
-            const bool before = stopped || ((m1mask & ((1ull << key) - 1ull)) != 0);
-            valid = !before && pos >= 0 && pos < qk.thr;
-          }
-          if (valid) {
-            const int lb = pos / args.cmp_block_size;
-            if (lb < args.cmp_table_len) {
-              const int blk =
-                  __ldg(args.cmp_block_table + (size_t)rv.b * args.cmp_table_len + lb);
-              if (blk >= 0 && blk < args.cmp_num_blocks) {
-                src = reinterpret_cast<const char*>(args.cmp_kv) +
-                      ((size_t)blk * args.cmp_block_size + (pos - lb * args.cmp_block_size)) *
-                          (size_t)D * 2;
-              } else if (blk >= args.cmp_num_blocks) {
-                record_error(err, SAS_ERR_DEVICE, 12, blk);
-              }
-            } else {
-              record_error(err, SAS_ERR_DEVICE, 13, pos);
-            }
-          }
-        }
+        // Slots resolved by this warp: LSU gather, keys 16 pw .. 16 pw + 15
+        // (lanes 16..31 mirror 0..15); TMA gather, all 64 keys (slot lane and
+        // slot lane + 32).
+        const int ka = lsu ? (pw * 16 + (lane & 15)) : lane;
+        const int kb = ka + 32;
+        const bool blk_a = stopped || ((m1mask & ((1ull << ka) - 1ull)) != 0);
+        const bool blk_b = stopped || ((m1mask & ((1ull << (kb & 63)) - 1ull)) != 0);
+        const SlotSrc sa = resolve_slot(args, rv, qk, j * kTileKeys + ka, idx_row, blk_a, err);
+        SlotSrc sb{-1, -1, false};
+        if (!lsu) sb = resolve_slot(args, rv, qk, j * kTileKeys + kb, idx_row, blk_b, err);
         if (m1mask != 0) stopped = true;
-        const uint32_t vbits = __ballot_sync(0xffffffffu, valid);
-        if (lane == 0) ctl.valid[stage][pw] = vbits;
-        __syncwarp();
-        mbar_arrive(smem_addr(&ctl.kv_full[stage]));
-        // Copy the 32 rows of this warp; zero rows where there is no source.
-        const uint32_t sK = sK0 + stage * kStageBytes;
-        for (int k = 0; k < 32; ++k) {
-          const char* s = reinterpret_cast<const char*>(
-              __shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(src), k));
-          const int row = pw * 32 + k;
-          const uint32_t nbytes = (s != nullptr) ? 16u : 0u;
-          const char* s_safe = (s != nullptr) ? s : reinterpret_cast<const char*>(args.ori_kv);
-          for (int gi = lane; gi < gran; gi += 32) {
-            cp_async_16(sK + (gi >> 3) * kChunkBytes + swz(row, gi & 7), s_safe + gi * 16,
-                        nbytes);
-          }
+        const uint32_t va = __ballot_sync(0xffffffffu, sa.valid);
+        const uint32_t vb = __ballot_sync(0xffffffffu, sb.valid);
+        if (leader && lane == 0) trace(tr, 0, 3 * produced);
+        if (!__all_sync(0xffffffffu,
+                        wait_bar(&ctl, &ctl.kv_empty[stage], kv_empty_par[stage], err, 2))) {
+          ok = false;
+          break;
         }
-        cp_async_arrive_noinc(smem_addr(&ctl.kv_full[stage]));
+        if (leader && lane == 0) trace(tr, 0, 3 * produced + 1);
+        kv_empty_par[stage] ^= 1u;
+        const uint32_t bar = smem_addr(&ctl.kv_full[stage]);
+        const uint32_t sK = sK0 + stage * kStageBytes;
+        if (lsu) {
+          if (lane == 0) ctl.valid[stage][pw] = (uint16_t)(va & 0xffffu);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar);
+          // 16 rows of this warp, 512 contiguous bytes per warp instruction;
+          // rows without a source are zero-filled (src size 0).
+          for (int k = 0; k < 16; ++k) {
+            const int row = __shfl_sync(0xffffffffu, sa.row, k);
+            const int pool = __shfl_sync(0xffffffffu, sa.pool, k);
+            const bool has = (pool >= 0 && row >= 0);
+            const char* src = reinterpret_cast<const char*>(pool == 1 ? args.cmp_kv : args.ori_kv);
+            if (has) src += (size_t)row * row_bytes;
+            else src = reinterpret_cast<const char*>(args.ori_kv);
+            const int key = pw * 16 + k;
+            for (int gi = lane; gi < gran; gi += 32)
+              cp_async_16(sK + (gi >> 3) * kChunkBytes + swz(key, gi & 7), src + gi * 16,
+                          has ? 16u : 0u);
+          }
+          cp_async_arrive_noinc(bar);
+        } else {
+          if (lane == 0) {
+            ctl.valid[stage][0] = (uint16_t)(va & 0xffffu);
+            ctl.valid[stage][1] = (uint16_t)(va >> 16);
+            ctl.valid[stage][2] = (uint16_t)(vb & 0xffffu);
+            ctl.valid[stage][3] = (uint16_t)(vb >> 16);
+            mbar_expect_tx(bar, kTileKeys * row_bytes);
+          }
+          __syncwarp();
+          issue_tile<false>(&tm_ori, &tm_cmp, args.ori_rows, args.cmp_rows, nchunks, sK, bar,
+                            lane, sa.row, sa.pool, sb.row, sb.pool);
+        }
+        if (leader && lane == 0) trace(tr, 0, 3 * produced + 2);
+        ++produced;
         stage ^= 1;
       }
     }
-    cp_async_wait_all();
+    if (lsu) cp_async_wait_all();
   } else if (warp == kMmaWarp) {
     // ======================= MMA issuer =======================
     if (lane == 0) {
@@ -489,27 +670,50 @@ __global__ void __launch_bounds__(kThreads, 1) sas_fwd_kernel(const FwdArgs args
       uint32_t kv_full_par[2] = {0u, 0u};
       uint32_t s_empty_par[2] = {1u, 1u};
       uint32_t q_full_par = 0u, p_full_par = 0u, o_free_par = 1u;
-      int stage = 0, sbuf = 0;
+      int stage = 0, sbuf = 0, pv_issued = 0;
       bool ok = true;
 
-      auto issue_qk = [&](int st, int sb) -> bool {
-        if (!wait_bar(&ctl, &ctl.kv_full[st], kv_full_par[st], err, 20)) return false;
-        kv_full_par[st] ^= 1u;
-        if (!wait_bar(&ctl, &ctl.s_empty[sb], s_empty_par[sb], err, 21)) return false;
-        s_empty_par[sb] ^= 1u;
+      // QK(j) into S buffer sb from K stage st (inputs already acquired).
+      int qk_issued = 0;
+      auto qk = [&](int st, int sb) {
+        trace(tr, 1, 2 * qk_issued);
+        ++qk_issued;
         fence_proxy_async();
         tc_fence_after();
-        const uint32_t d = tmem + kTmemS + 32u * sb;
+        // Chunk c accumulates into partial c % 4; consecutive MMAs rotate
+        // over the partials so four dependent chains overlap in the pipe.
+        const uint32_t d = tmem + kTmemS + 128u * sb;
         const uint32_t kb = sK0 + st * kStageBytes;
-        for (int c = 0; c < nchunks; ++c) {
+        for (int c4 = 0; c4 < nchunks; c4 += kQkPartials) {
           for (int ks = 0; ks < 4; ++ks) {
-            const uint64_t a = smem_desc(sQ + c * kChunkBytes + ks * 32, 16, 1024);
-            const uint64_t b = smem_desc(kb + c * kChunkBytes + ks * 32, 16, 1024);
-            mma_ws(d, a, b, idesc_qk, (c | ks) != 0 ? 1u : 0u);
+            for (int pp = 0; pp < kQkPartials; ++pp) {
+              const int c = c4 + pp;
+              if (c >= nchunks) break;
+              const uint64_t a = smem_desc(sQ + c * kChunkBytes + ks * 32, 16, 1024);
+              const uint64_t b = smem_desc(kb + c * kChunkBytes + ks * 32, 16, 1024);
+              mma_ws(d + 32u * pp, a, b, idesc_qk, (c4 == 0 && ks == 0) ? 0u : 1u);
+            }
           }
         }
         tc_commit(smem_addr(&ctl.s_full[sb]));
-        return true;
+      };
+      // O (+)= P V for the tile in K stage st.
+      auto pv = [&](int st, bool first) {
+        trace(tr, 1, 2 * pv_issued + 1);
+        fence_proxy_async();
+        tc_fence_after();
+        const uint32_t kb = sK0 + st * kStageBytes;
+        for (int ks = 0; ks < 4; ++ks) {
+          const uint64_t a = smem_desc(kb + kPChunk * kChunkBytes + ks * 32, 16, 1024);
+          for (int hv = 0; hv < 2; ++hv) {
+            const uint64_t b =
+                smem_desc(kb + (4 * hv) * kChunkBytes + ks * 2048, kChunkBytes, 1024);
+            mma_ws(tmem + kTmemO + 128u * hv, a, b, idesc_pv, (first && ks == 0) ? 0u : 1u);
+          }
+        }
+        tc_commit(smem_addr(&ctl.kv_empty[st]));
+        tc_commit(smem_addr(&ctl.pv_done[pv_issued & 1]));
+        ++pv_issued;
       };
 
       for (int r = span.r0; ok && span.r0 >= 0 && r <= span.r1; ++r) {
@@ -520,38 +724,64 @@ __global__ void __launch_bounds__(kThreads, 1) sas_fwd_kernel(const FwdArgs args
         if (tiles == 0 || ja >= jb) continue;
         if (!wait_bar(&ctl, &ctl.q_full, q_full_par, err, 22)) { ok = false; break; }
         q_full_par ^= 1u;
-        int st_next = stage, sb_next = sbuf;
-        if (!issue_qk(st_next, sb_next)) { ok = false; break; }
+        if (!wait_bar(&ctl, &ctl.kv_full[stage], kv_full_par[stage], err, 20)) { ok = false; break; }
+        kv_full_par[stage] ^= 1u;
+        if (!wait_bar(&ctl, &ctl.s_empty[sbuf], s_empty_par[sbuf], err, 21)) { ok = false; break; }
+        s_empty_par[sbuf] ^= 1u;
+        qk(stage, sbuf);
         if (jb - ja == 1) tc_commit(smem_addr(&ctl.q_empty));
-        for (int j = ja; j < jb; ++j) {
-          const int st = stage, sb = sbuf;
+        for (int j = ja; j < jb && ok; ++j) {
+          const int st = stage;
           stage ^= 1;
           sbuf ^= 1;
-          if (j + 1 < jb) {
-            if (!issue_qk(stage, sbuf)) { ok = false; break; }
-            if (j + 2 == jb) tc_commit(smem_addr(&ctl.q_empty));
-          }
-          if (!wait_bar(&ctl, &ctl.p_full, p_full_par, err, 23)) { ok = false; break; }
-          p_full_par ^= 1u;
-          if (j == ja) {
-            if (!wait_bar(&ctl, &ctl.o_free, o_free_par, err, 24)) { ok = false; break; }
-            o_free_par ^= 1u;
-          }
-          fence_proxy_async();
-          tc_fence_after();
-          const uint32_t kb = sK0 + st * kStageBytes;
-          for (int ks = 0; ks < 4; ++ks) {
-            const uint64_t a = smem_desc(sP + ks * 32, 16, 1024);
-            for (int hv = 0; hv < 2; ++hv) {
-              const uint64_t b =
-                  smem_desc(kb + (4 * hv) * kChunkBytes + ks * 2048, kChunkBytes, 1024);
-              mma_ws(tmem + kTmemO + 128u * hv, a, b, idesc_pv,
-                     (j == ja && ks == 0) ? 0u : 1u);
+          // Issue QK(j+1) and PV(j) in whichever order their inputs arrive
+          // (QK first when both are ready, so softmax(j+1) overlaps PV(j)).
+          bool need_qk = (j + 1 < jb), kv_ok = false, s_ok = false;
+          bool need_pv = true, p_ok = false, o_ok = (j != ja);
+          long long t0 = clock64();
+          while (need_qk || need_pv) {
+            bool progress = false;
+            if (need_qk) {
+              if (!kv_ok && mbar_test(smem_addr(&ctl.kv_full[stage]), kv_full_par[stage])) {
+                kv_ok = true;
+                kv_full_par[stage] ^= 1u;
+              }
+              if (!s_ok && mbar_test(smem_addr(&ctl.s_empty[sbuf]), s_empty_par[sbuf])) {
+                s_ok = true;
+                s_empty_par[sbuf] ^= 1u;
+              }
+              if (kv_ok && s_ok) {
+                qk(stage, sbuf);
+                if (j + 2 == jb) tc_commit(smem_addr(&ctl.q_empty));
+                need_qk = false;
+                progress = true;
+              }
+            }
+            if (need_pv) {
+              if (!p_ok && mbar_test(smem_addr(&ctl.p_full), p_full_par)) {
+                p_ok = true;
+                p_full_par ^= 1u;
+              }
+              if (!o_ok && mbar_test(smem_addr(&ctl.o_free), o_free_par)) {
+                o_ok = true;
+                o_free_par ^= 1u;
+              }
+              if (p_ok && o_ok) {
+                pv(st, j == ja);
+                need_pv = false;
+                progress = true;
+              }
+            }
+            if (!progress) {
+              if (ctl.abort) { ok = false; break; }
+              if (clock64() - t0 > kWaitCycles) {
+                record_error(err, SAS_ERR_DEVICE, 23, j);
+                ctl.abort = 1;
+                ok = false;
+                break;
+              }
             }
           }
-          tc_commit(smem_addr(&ctl.kv_empty[st]));
-          tc_commit(smem_addr(&ctl.pv_done));
-          (void)sb;
         }
       }
       // Drain: the commit arrives once every MMA issued above has finished,
@@ -572,7 +802,17 @@ __global__ void __launch_bounds__(kThreads, 1) sas_fwd_kernel(const FwdArgs args
     const float sink = live ? __ldg(args.sinks + head) : -INFINITY;
     uint32_t kv_full_par[2] = {0u, 0u};
     uint32_t s_full_par[2] = {0u, 0u};
-    uint32_t pv_done_par = 0u;
+    int pv_count = 0;  // PVs released by this thread's p_full arrivals so far
+    int rows_done = 0;
+    // Completion of PV number k: phase k/2 of pv_done[k % 2].  When softmax
+    // waits for PV k, PV k-2 is complete (the S of the current tile is only
+    // produced after the PV two tiles back freed its K stage) and PV k+2 is
+    // not yet released, so pv_done[k % 2] is exactly one phase short of or
+    // at the awaited completion and the parity test is exact, although most
+    // completions are never waited for.
+    auto wait_pv = [&](int k, int site) -> bool {
+      return wait_bar(&ctl, &ctl.pv_done[k & 1], (uint32_t)((k >> 1) & 1), err, site);
+    };
     uint32_t xph[2] = {0u, 0u};
     int stage = 0, sbuf = 0, xpar = 0;
     // Partner exchange through ctl.red[xpar], ordered by the bounded
@@ -614,13 +854,33 @@ __global__ void __launch_bounds__(kThreads, 1) sas_fwd_kernel(const FwdArgs args
         s_full_par[sb] ^= 1u;
         if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.kv_full[st], kv_full_par[st], err, 31))) { ok = false; break; }
         kv_full_par[st] ^= 1u;
+        if (threadIdx.x == 0) trace(tr, 2, 4 * pv_count);
         tc_fence_after();
         uint32_t sraw[32];
-        tmem_ld32(tmem + lane_off + kTmemS + 32u * sb, sraw);
-        tmem_wait_ld();
+        {
+          const uint32_t ts = tmem + lane_off + kTmemS + 128u * sb;
+          uint32_t t1[32];
+          tmem_ld32(ts, sraw);
+          tmem_ld32(ts + 32u, t1);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            sraw[i] = __float_as_uint(__uint_as_float(sraw[i]) + __uint_as_float(t1[i]));
+          tmem_ld32(ts + 64u, t1);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            sraw[i] = __float_as_uint(__uint_as_float(sraw[i]) + __uint_as_float(t1[i]));
+          tmem_ld32(ts + 96u, t1);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            sraw[i] = __float_as_uint(__uint_as_float(sraw[i]) + __uint_as_float(t1[i]));
+        }
         tc_fence_before();
         mbar_arrive(smem_addr(&ctl.s_empty[sb]));
-        const uint32_t vb = ctl.valid[st][half];
+        const uint32_t vb = (uint32_t)ctl.valid[st][2 * half] |
+                            ((uint32_t)ctl.valid[st][2 * half + 1] << 16);
         float x[32];
         float mx = -INFINITY;
 #pragma unroll
@@ -633,6 +893,7 @@ __global__ void __launch_bounds__(kThreads, 1) sas_fwd_kernel(const FwdArgs args
         if (!__all_sync(0xffffffffu, exchange(34))) { ok = false; break; }
         mx = fmaxf(mx, ctl.red[xpar][half ^ 1][m]);
         xpar ^= 1;
+        if (threadIdx.x == 0) trace(tr, 2, 4 * pv_count + 1);
         const float m_new = fmaxf(m_run, mx);
         const bool rescale = (m_new - m_run) > kRescaleThreshold;  // NaN (-inf,-inf) -> false
         float alpha = 1.f;
@@ -652,39 +913,47 @@ __global__ void __launch_bounds__(kThreads, 1) sas_fwd_kernel(const FwdArgs args
           pk[i / 2] = pack2<kBf16>(p0, p1);
         }
         l_run += lsum;
-        if (j > ja) {
-          if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.pv_done, pv_done_par, err, 32))) { ok = false; break; }
-          pv_done_par ^= 1u;
-          tc_fence_after();
-          if (__any_sync(0xffffffffu, rescale)) {
-            // O *= alpha for this thread's 256 accumulator columns.
-            for (int c = 0; c < 8; ++c) {
-              const uint32_t ta = tmem + lane_off + kTmemO + 32u * c;
-              uint32_t v[32];
-              tmem_ld32(ta, v);
-              tmem_wait_ld();
-#pragma unroll
-              for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-              tmem_st32(ta, v);
-            }
-            tmem_wait_st();
-          }
-        }
-        // P row m, keys [32*half, 32*half + 32) -> granules 4*half .. 4*half+3.
-        uint8_t* prow = gbase + kSmemP;
+        // P(j) into chunk 8 of tile j's own stage (free: S(j) is complete).
+        uint8_t* prow = gbase + kSmemK0 + st * kStageBytes + kPChunk * kChunkBytes;
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
           uint4 v = make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
           *reinterpret_cast<uint4*>(prow + swz(m, 4 * half + g)) = v;
         }
         fence_proxy_async();
+        // The running max moved by more than the lazy threshold: O must be
+        // rescaled after PV(j-1) (number pv_count - 1) and before PV(j).
+        if (j > ja && __any_sync(0xffffffffu, rescale)) {
+          if (!__all_sync(0xffffffffu, wait_pv(pv_count - 1, 32))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          for (int c = 0; c < 8; ++c) {
+            const uint32_t ta = tmem + lane_off + kTmemO + 32u * c;
+            uint32_t v[32];
+            tmem_ld32(ta, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+            tmem_st32(ta, v);
+          }
+          tmem_wait_st();
+        }
         tc_fence_before();
+        if (threadIdx.x == 0) trace(tr, 2, 4 * pv_count + 2);
         mbar_arrive(smem_addr(&ctl.p_full));
+        ++pv_count;
       }
       if (!ok) break;
       // ---- epilogue of this (row, piece) ----
-      if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.pv_done, pv_done_par, err, 33))) { ok = false; break; }
-      pv_done_par ^= 1u;
+      if (threadIdx.x == 0) trace(tr, 3, 2 * rows_done);
+      if (!__all_sync(0xffffffffu, wait_pv(pv_count - 1, 33))) {
+        ok = false;
+        break;
+      }
+      if (threadIdx.x == 0) trace(tr, 3, 2 * rows_done + 1);
+      ++rows_done;
       tc_fence_after();
       ctl.red[xpar][half][m] = l_run;
       if (!__all_sync(0xffffffffu, exchange(35))) { ok = false; break; }
@@ -747,6 +1016,37 @@ __global__ void __launch_bounds__(kThreads, 1) sas_fwd_kernel(const FwdArgs args
 
 }  // namespace
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no
+// link-time dependency on libcuda).
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2D map over a row-major [rows, cols] 16-bit matrix with a (64 x box_rows)
+// box, 128-byte swizzle, zero fill out of range.
+static bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols,
+                     uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (fn == nullptr || base == nullptr || rows == 0) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 int launch_fwd(const FwdArgs& args, int grid, cudaStream_t stream) {
   static bool configured[2] = {false, false};
   const bool bf16 = args.dtype == SAS_DTYPE_BF16;
@@ -757,10 +1057,20 @@ int launch_fwd(const FwdArgs& args, int grid, cudaStream_t stream) {
     if (e != cudaSuccess) return SAS_ERR_CUDA;
     configured[bf16 ? 0 : 1] = true;
   }
+  alignas(64) CUtensorMap tm_q, tm_ori, tm_cmp;
+  const uint64_t D = (uint64_t)args.head_dim;
+  if (!make_map(&tm_q, args.q, (uint64_t)args.total_tokens * args.num_heads, D, kHeadsPerCta))
+    return SAS_ERR_CUDA;
+  if (!make_map(&tm_ori, args.ori_kv, (uint64_t)args.ori_rows, D, 1)) return SAS_ERR_CUDA;
+  if (args.cmp_kv != nullptr && args.cmp_rows > 0) {
+    if (!make_map(&tm_cmp, args.cmp_kv, (uint64_t)args.cmp_rows, D, 1)) return SAS_ERR_CUDA;
+  } else {
+    tm_cmp = tm_ori;
+  }
   if (bf16)
-    sas_fwd_kernel<true><<<grid, kThreads, kSmemDynamic, stream>>>(args);
+    sas_fwd_kernel<true><<<grid, kThreads, kSmemDynamic, stream>>>(args, tm_q, tm_ori, tm_cmp);
   else
-    sas_fwd_kernel<false><<<grid, kThreads, kSmemDynamic, stream>>>(args);
+    sas_fwd_kernel<false><<<grid, kThreads, kSmemDynamic, stream>>>(args, tm_q, tm_ori, tm_cmp);
   return cudaGetLastError() == cudaSuccess ? SAS_OK : SAS_ERR_CUDA;
 }
 

@@ -21,6 +21,7 @@ struct FwdArgs {
   void* out;
   float* lse;
   int32_t* err;
+  long long* trace;         // optional clock trace of CTA 0 (diagnostics)
   const int32_t* plan;      // device copy of the serialised plan
   const int32_t* q_len;     // [B] device (act_q per batch)
   const int32_t* kv_len;    // [B] device (seqused_kv)
@@ -32,6 +33,10 @@ struct FwdArgs {
   int32_t ori_block_size, ori_num_blocks, ori_table_len;
   int32_t cmp_block_size, cmp_num_blocks, cmp_table_len;
   int32_t head_groups;
+  int32_t total_tokens;     // rows of q (for the Q tensor map)
+  int32_t ori_rows;         // ori_num_blocks * ori_block_size (out-of-range row = zero fill)
+  int32_t cmp_rows;         // cmp_num_blocks * cmp_block_size
+  int32_t gather;           // key-row gather: 0 = cp.async (LSU), 1 = TMA gather4
 };
 
 int launch_fwd(const FwdArgs& args, int grid, cudaStream_t stream);
