@@ -83,10 +83,25 @@ def _dev_i32(t: torch.Tensor, device) -> torch.Tensor:
     return t.to(device=device, dtype=torch.int32).contiguous()
 
 
-def _forward(q: torch.Tensor, *, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table,
-             cmp_block_table, cu_seqlens_q, seqused_kv, sinks, softmax_scale, cmp_ratio,
-             ori_win_left, layout_q, topk_cmp, head_dim_v, num_sms, err=None):
-    """Shared implementation of both entry points; returns flat (out, lse)."""
+class CallArgs:
+    """C-ABI argument blocks of one forward call (``SasProblem`` +
+    ``SasFwdParams``), the flat outputs they point to, and every buffer the
+    pointers reference (kept alive with the object)."""
+
+    def __init__(self, **kw):
+        self.__dict__.update(kw)
+
+
+def build_call(q: torch.Tensor, *, ori_kv, cmp_kv=None, cmp_sparse_indices=None,
+               ori_block_table, cmp_block_table=None, cu_seqlens_q=None, seqused_kv,
+               sinks, softmax_scale, cmp_ratio=None, ori_win_left=127, layout_q="TND",
+               topk_cmp=None, head_dim_v=None, num_sms=None, err=None) -> CallArgs:
+    """Validate the reference-style arguments and build the C-ABI structs.
+
+    Mirrors api.py:196-366 (scenario resolution, TND/BSND flattening, K
+    resolution, shape checks); allocates the flat ``out [T, N1, d_v]`` and
+    ``lse [T, N1]`` that ``sas_fwd`` writes.
+    """
     dtype = q.dtype
     dcode = _dtype_code(dtype)
     dev = q.device
@@ -213,15 +228,25 @@ def _forward(q: torch.Tensor, *, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_t
         fp.cmp_block_size, fp.cmp_num_blocks = cmp.shape[1], cmp.shape[0]
         fp.cmp_table_len = cmp_bt.shape[1]
     fp.num_sms = int(num_sms or 0)
+    return CallArgs(prob=prob, fp=fp, out=out, lse=lse, total=total, device=dev,
+                    plan_key=(layout_q, tuple(q_start), tuple(q_len), tuple(kv_len), N1,
+                              scenario, int(ori_win_left), ratio, int(K), fp.num_sms, total,
+                              S_max),
+                    keep=(q_flat, ori, ori_bt, cmp, cmp_bt, idx, snk, err, a_start, a_len,
+                          a_kv))
 
+
+def _forward(q: torch.Tensor, **kw):
+    """Shared implementation of both entry points; returns flat (out, lse)."""
     global last_plan_info
+    call = build_call(q, **kw)
+    prob, fp, out, lse, dev = call.prob, call.fp, call.out, call.lse, call.device
     L = _lib.lib()
-    if total == 0:
+    if call.total == 0:
         return out, lse
     with torch.cuda.device(dev):
         stream = torch.cuda.current_stream(dev).cuda_stream
-        key = (dev.index, stream, layout_q, tuple(q_start), tuple(q_len), tuple(kv_len), N1,
-               scenario, int(ori_win_left), ratio, int(K), fp.num_sms, total, S_max)
+        key = (dev.index, stream) + call.plan_key
         hit = _PLAN_CACHE.get(key)
         if hit is None:
             ws_bytes = C.c_size_t(0)
