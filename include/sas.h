@@ -166,6 +166,21 @@ int sas_fwd_prepare(const SasProblem* prob, const SasFwdParams* params, void* wo
 int sas_fwd_execute(const SasProblem* prob, const SasFwdParams* params, const SasPlanInfo* info,
                     void* workspace, size_t workspace_bytes, void* stream, int32_t phases);
 
+/* Forward without a caller workspace, for callers that cannot allocate
+ * device memory (an arena planned ahead of time, an allocator frozen during a
+ * step, a host that forbids allocation after start-up).  No counterpart in
+ * the reference: its jit runtime always owns the workspaces.
+ * The plan and split-KV partials live in a file-scope device array of
+ * SAS_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until
+ * exit; a problem needing more returns SAS_ERR_WORKSPACE (fewer workers via
+ * params->num_sms shrink the partials).  The array's device address is set
+ * up on a device's first call: make that call before any stream capture.
+ * All calls on a device share the array (it keeps the last call's contents;
+ * nothing in it needs to start at zero), so calls that overlap on the GPU
+ * race: serialise them.  Makes no device allocation. */
+#define SAS_NOALLOC_SCRATCH_BYTES (16u << 20)
+int sas_fwd_noalloc(const SasProblem* prob, const SasFwdParams* params, void* stream);
+
 /* LSE-combine of split-KV partials (normally called by sas_fwd).  For each of
  * `num_rows` split rows, piece i of row r is partial slot `partial_base[r]+i`:
  * o_partial [slots, H, d_v] fp32 (normalised), lse_partial [slots, H] fp32.

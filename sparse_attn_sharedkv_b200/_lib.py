@@ -22,6 +22,7 @@ DTYPE_BF16, DTYPE_FP16 = 0, 1
 SCENARIO_SWA, SCENARIO_CFA, SCENARIO_SCFA = 1, 2, 3
 PHASE_ATTN, PHASE_COMBINE, PHASE_ALL = 1, 2, 3
 SAS_META_SIZE = 1024
+SAS_NOALLOC_SCRATCH_BYTES = 16 << 20
 SAS_AIC_CORE_NUM = 36
 SAS_AIV_CORE_NUM = 72
 SAS_FA_METADATA_SIZE = 8
@@ -94,6 +95,8 @@ PROTOTYPES = {
     "sas_fwd_execute": (C.c_int, [C.POINTER(SasProblem), C.POINTER(SasFwdParams),
                                   C.POINTER(SasPlanInfo), C.c_void_p, C.c_size_t, C.c_void_p,
                                   C.c_int32]),
+    "sas_fwd_noalloc": (C.c_int, [C.POINTER(SasProblem), C.POINTER(SasFwdParams),
+                                  C.c_void_p]),
     "sas_combine": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p,
                               C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
                               C.c_void_p, C.c_void_p]),
