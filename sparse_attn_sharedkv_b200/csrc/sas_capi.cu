@@ -161,12 +161,12 @@ extern "C" int sas_fwd_execute(const SasProblem* prob, const SasFwdParams* param
   a.ori_rows = f.ori_num_blocks * f.ori_block_size;
   a.cmp_rows = f.cmp_kv ? f.cmp_num_blocks * a.cmp_block_size : 0;
   {
-    // Key-row gather engine: cp.async from four warps (default) or TMA
-    // tile::gather4 (SAS_GATHER=tma).
+    // Key-row gather engine: TMA tile::gather4 from the four producer warps
+    // (default) or cp.async 16 B (SAS_GATHER=lsu).
     static int gather = -1;
     if (gather < 0) {
       const char* e = getenv("SAS_GATHER");
-      gather = (e != nullptr && strcmp(e, "tma") == 0) ? 1 : 0;
+      gather = (e != nullptr && strcmp(e, "lsu") == 0) ? 0 : 1;
     }
     a.gather = gather;
   }

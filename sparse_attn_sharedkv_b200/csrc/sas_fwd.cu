@@ -9,13 +9,15 @@
 // Per tile of 64 key slots (window keys then compressed keys, golden.py
 // tile order) the CTA runs:
 //
-//   producer warp      slot -> (cache, logical pos) -> block table -> row;
-//                      TMA tile::gather4 of 4 rows x 128 B per op into a
-//                      128B-swizzled K tile (paged window load, kernel.py:
-//                      3580-3600, and top-k gather, kernel.py:2606-2751),
-//                      -1 stop / threshold masks (golden.py:28-66) into a
-//                      per-tile valid mask; Q tiles by 64 x 64 TMA boxes
-//   prefetch warp      the same rows a few tiles ahead, into L2
+//   producer warps (4)  slot -> (cache, logical pos) -> block table -> row
+//                       for 16 keys each; TMA tile::gather4 of 4 rows x 128 B
+//                       per op into a 128B-swizzled K tile, issued from all
+//                       four warps (TMA issue is per-warp serial, so four
+//                       issuing warps move ~2.7x the bytes of one) (paged
+//                       window load, kernel.py:3580-3600, and top-k gather,
+//                       kernel.py:2606-2751); -1 stop / threshold masks
+//                       (golden.py:28-66) into a per-tile valid mask; Q tiles
+//                       by 64 x 64 TMA boxes
 //   MMA warp (1 lane)   S = Q K^T  : 36 x tcgen05.mma.ws M64 N64 K16 (d_qk 576)
 //                       O += P V   : 8 x tcgen05.mma.ws M64 N256 K16, where V is
 //                                    the same smem K tile read MN-major (d_v 512)
@@ -50,10 +52,11 @@ namespace sas {
 namespace {
 
 constexpr int kNumSoftmaxWarps = 4;
-constexpr int kProducerWarp0 = 4;  // producer warps 4..7; warp 4 also loads Q by TMA
+constexpr int kProducerWarp0 = 4;  // producer warps 4..7 gather key rows
 constexpr int kNumProducerWarps = 4;
 constexpr int kMmaWarp = 8;
-constexpr int kThreads = 32 * 9;
+constexpr int kQWarp = 9;          // loads Q tiles by TMA, prefetches the next row's Q into L2
+constexpr int kThreads = 32 * 10;
 constexpr int kSoftmaxThreads = 32 * kNumSoftmaxWarps;
 constexpr int kProducerThreads = 32 * kNumProducerWarps;
 constexpr int kQkPartials = 4;     // independent S accumulators per tile (QK chains)
@@ -71,7 +74,7 @@ constexpr int kSmemDynamic = kSmemTiles + 1024;        // + runtime 1 KB alignme
 // it is free once S(j) is complete and is double-buffered with the stages.
 constexpr int kPChunk = 8;
 constexpr int kGatherLsu = 0;  // key rows by cp.async 16 B from the 4 producer warps
-constexpr int kGatherTma = 1;  // key rows by TMA tile::gather4 from producer warp 4
+constexpr int kGatherTma = 1;  // key rows by TMA tile::gather4 from the 4 producer warps
 
 // TMEM columns.
 constexpr uint32_t kTmemCols = 512;
@@ -410,28 +413,43 @@ __device__ __forceinline__ SlotSrc resolve_slot(const FwdArgs& a, const Row& rv,
   return r;
 }
 
-// Issue (or L2-prefetch) the key rows of one 64-slot tile.  Lane l holds
-// slot l in (ra, pa) and slot l + 32 in (rb, pb).  Lanes 0..15 each move a
-// group of 4 consecutive slots with one tile::gather4 per 64-column chunk;
-// a group whose rows come from both caches falls back to single-row tiled
-// loads.  Rows without a source use an out-of-range row: TMA fills zeros.
-template <bool kPrefetch>
-__device__ __forceinline__ void issue_tile(const CUtensorMap* tm_ori, const CUtensorMap* tm_cmp,
-                                           int ori_rows, int cmp_rows, int nchunks,
-                                           uint32_t stage_base, uint32_t bar, int lane, int ra,
-                                           int pa, int rb, int pb) {
-  const int g = lane & 15;
+// cp.async of `count` key rows of this warp's 16-key block: local key
+// lbase + k (k < count) sits at smem row key0 + lbase + k and its source is
+// (r, p) of lane lbase + k.  Rows without a source are zero-filled (src-size 0).
+__device__ __forceinline__ void lsu_rows(const FwdArgs& a, uint32_t sK, int key0, int lbase,
+                                         int count, int r, int p, int lane, uint32_t row_bytes,
+                                         int gran) {
+  for (int k = 0; k < count; ++k) {
+    const int row = __shfl_sync(0xffffffffu, r, lbase + k);
+    const int pool = __shfl_sync(0xffffffffu, p, lbase + k);
+    const bool has = (pool >= 0 && row >= 0);
+    const char* src = reinterpret_cast<const char*>(pool == 1 ? a.cmp_kv : a.ori_kv);
+    if (has) src += (size_t)row * row_bytes;
+    else src = reinterpret_cast<const char*>(a.ori_kv);
+    const int key = key0 + lbase + k;
+    for (int gi = lane; gi < gran; gi += 32)
+      cp_async_16(sK + (gi >> 3) * kChunkBytes + swz(key, gi & 7), src + gi * 16,
+                  has ? 16u : 0u);
+  }
+}
+
+// TMA gather of this warp's 16 key rows (smem rows key0 .. key0 + 15): lanes
+// 0..3 each move a group of 4 consecutive keys with one tile::gather4 per
+// 64-column chunk (4 rows x 128 B into 512 B of the swizzled chunk).  Slots
+// without a source read an out-of-range row, which TMA fills with zeros.  A
+// group whose rows come from both caches (window / compressed boundary) is
+// moved by cp.async instead.  Lane 0 arms the barrier with the TMA bytes.
+__device__ __forceinline__ void tma_rows(const FwdArgs& a, const CUtensorMap* tm_ori,
+                                         const CUtensorMap* tm_cmp, int nchunks, uint32_t sK,
+                                         uint32_t bar, int key0, int r, int p, int lane,
+                                         uint32_t row_bytes, int gran) {
+  const int g = lane & 3;
   int row[4], pool[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const int key = 4 * g + i;
-    const int src = key & 31;
-    const int xa = __shfl_sync(0xffffffffu, ra, src), xb = __shfl_sync(0xffffffffu, rb, src);
-    const int ya = __shfl_sync(0xffffffffu, pa, src), yb = __shfl_sync(0xffffffffu, pb, src);
-    row[i] = key < 32 ? xa : xb;
-    pool[i] = key < 32 ? ya : yb;
+    row[i] = __shfl_sync(0xffffffffu, r, 4 * g + i);
+    pool[i] = __shfl_sync(0xffffffffu, p, 4 * g + i);
   }
-  if (lane >= 16) return;
   int P = -1;
   bool mixed = false;
 #pragma unroll
@@ -441,30 +459,70 @@ __device__ __forceinline__ void issue_tile(const CUtensorMap* tm_ori, const CUte
       else if (pool[i] != P) mixed = true;
     }
   }
-  const uint32_t dst = stage_base + g * 4 * 128;
-  if (!mixed) {
+  const uint32_t mixed_mask = __ballot_sync(0xffffffffu, mixed) & 0xFu;
+  if (lane == 0) mbar_expect_tx(bar, (uint32_t)(4 - __popc(mixed_mask)) * 4u * row_bytes);
+  __syncwarp();
+  if (lane < 4 && !mixed) {
     const CUtensorMap* m = (P == 1) ? tm_cmp : tm_ori;
-    const int sentinel = (P == 1) ? cmp_rows : ori_rows;
+    const int sentinel = (P == 1) ? a.cmp_rows : a.ori_rows;
 #pragma unroll
     for (int i = 0; i < 4; ++i)
       if (pool[i] < 0 || row[i] < 0) row[i] = sentinel;
-    for (int c = 0; c < nchunks; ++c) {
-      if constexpr (kPrefetch)
-        tma_prefetch_gather4(m, c * 64, row[0], row[1], row[2], row[3]);
-      else
-        tma_gather4(dst + c * kChunkBytes, m, c * 64, row[0], row[1], row[2], row[3], bar);
-    }
-  } else {
+    const uint32_t dst = sK + (uint32_t)(key0 + 4 * lane) * 128u;
+    for (int c = 0; c < nchunks; ++c)
+      tma_gather4(dst + c * kChunkBytes, m, c * 64, row[0], row[1], row[2], row[3], bar);
+  }
+  for (uint32_t mm = mixed_mask; mm != 0u; mm &= mm - 1u)
+    lsu_rows(a, sK, key0, 4 * (__ffs(mm) - 1), 4, r, p, lane, row_bytes, gran);
+}
+
+// S[sb] = Q K^T for the K tile at kb: chunk c accumulates into partial c % 4
+// and consecutive MMAs rotate over the partials, so four dependent chains
+// overlap in the pipe.  Descriptors are built once and advanced by constant
+// offsets (all shared addresses are below 256 KB, so the 14-bit address
+// field never carries).  Fully unrolled: the issuing thread spends a few
+// instructions per MMA.
+template <int kChunks>
+__device__ __forceinline__ void issue_qk(uint32_t d, uint32_t sQ, uint32_t kb, uint32_t idesc) {
+  const uint64_t dq = smem_desc(sQ, 16, 1024);
+  const uint64_t dk = smem_desc(kb, 16, 1024);
+#pragma unroll 1
+  for (int c4 = 0; c4 < kChunks; c4 += kQkPartials) {
+    const uint64_t c4off = (uint64_t)((c4 * kChunkBytes) >> 4);
+    const uint32_t acc0 = c4 == 0 ? 0u : 1u;
+    if (c4 + kQkPartials <= kChunks) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const CUtensorMap* m = (pool[i] == 1) ? tm_cmp : tm_ori;
-      const int y = row[i] >= 0 ? row[i] : ((pool[i] == 1) ? cmp_rows : ori_rows);
-      for (int c = 0; c < nchunks; ++c) {
-        if constexpr (kPrefetch)
-          tma_prefetch_2d(m, c * 64, y);
-        else
-          tma_load_2d(dst + c * kChunkBytes + i * 128, m, c * 64, y, bar);
+      for (int ks = 0; ks < 4; ++ks) {
+#pragma unroll
+        for (int pp = 0; pp < kQkPartials; ++pp) {
+          const uint64_t off = c4off + (uint64_t)((pp * kChunkBytes + ks * 32) >> 4);
+          mma_ws(d + 32u * pp, dq + off, dk + off, idesc, ks == 0 ? acc0 : 1u);
+        }
       }
+    } else {
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        for (int pp = 0; pp < kChunks - c4; ++pp) {
+          const uint64_t off = c4off + (uint64_t)((pp * kChunkBytes + ks * 32) >> 4);
+          mma_ws(d + 32u * pp, dq + off, dk + off, idesc, ks == 0 ? acc0 : 1u);
+        }
+      }
+    }
+  }
+}
+
+// O (+)= P V for the K tile at kb: P (64 x 64) from the rope chunk, V = dims
+// 0..511 of the same tile read MN-major, two N = 256 halves.
+__device__ __forceinline__ void issue_pv(uint32_t o, uint32_t kb, uint32_t idesc, bool first) {
+  const uint64_t dp = smem_desc(kb + kPChunk * kChunkBytes, 16, 1024);
+  const uint64_t dv = smem_desc(kb, kChunkBytes, 1024);
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks) {
+#pragma unroll
+    for (int hv = 0; hv < 2; ++hv) {
+      const uint64_t boff = (uint64_t)((4 * hv * kChunkBytes + ks * 2048) >> 4);
+      mma_ws(o + 128u * hv, dp + (uint64_t)((ks * 32) >> 4), dv + boff, idesc,
+             (first && ks == 0) ? 0u : 1u);
     }
   }
 }
@@ -473,7 +531,7 @@ __device__ __forceinline__ void issue_tile(const CUtensorMap* tm_ori, const CUte
 // The kernel.
 // ---------------------------------------------------------------------------
 
-template <bool kBf16>
+template <bool kBf16, int kChunks>
 __global__ void __launch_bounds__(kThreads, 1)
     sas_fwd_kernel(const FwdArgs args, const __grid_constant__ CUtensorMap tm_q,
                    const __grid_constant__ CUtensorMap tm_ori,
@@ -488,7 +546,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int group = blockIdx.x % hg;
   const int* plan = args.plan;
   const int* rows = plan + plan[H_ROWS_OFF];
-  const int nchunks = args.head_dim >> 6;
+  constexpr int nchunks = kChunks;  // d_qk / 64
   int* err = args.err;
   long long* tr = args.trace;
 
@@ -501,10 +559,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
-      // LSU gather: 4 warp arrivals (valid bits written) + 128 cp.async
-      // completions; TMA gather: one arrive.expect_tx.
-      mbar_init(smem_addr(&ctl.kv_full[i]),
-                args.gather == kGatherLsu ? kNumProducerWarps + kProducerThreads : 1);
+      // Per producer warp: one arrival from lane 0 after the valid bits are
+      // written (arming the TMA bytes in TMA mode) and one cp.async
+      // completion arrival per lane.
+      mbar_init(smem_addr(&ctl.kv_full[i]), kNumProducerWarps + kProducerThreads);
       mbar_init(smem_addr(&ctl.kv_empty[i]), 1);
       mbar_init(smem_addr(&ctl.s_full[i]), 1);
       mbar_init(smem_addr(&ctl.s_empty[i]), kSoftmaxThreads);
@@ -544,8 +602,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int D = args.head_dim;
     const uint32_t row_bytes = (uint32_t)D * 2u;
     const int gran = D >> 3;  // 16-byte granules per row
-    uint32_t kv_empty_par[2] = {1u, 1u};
-    uint32_t q_empty_par = 1u;
+    uint32_t kv_empty_par = 3u;  // bit = stage
     int stage = 0, produced = 0;
     bool ok = true;
     for (int r = span.r0; ok && span.r0 >= 0 && r <= span.r1; ++r) {
@@ -554,22 +611,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int ja = (r == span.r0) ? span.t0 : 0;
       const int jb = (r == span.r1) ? span.t1 : (tiles > 0 ? tiles : 1);
       if (tiles == 0 || ja >= jb) continue;
-      if (!lsu && !leader) continue;  // TMA gather: warp 4 alone
-      // ---- Q tile: 64 heads of this group, one 64 x 64 TMA box per chunk ----
-      if (leader) {
-        if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.q_empty, q_empty_par, err, 1))) {
-          ok = false;
-          break;
-        }
-        q_empty_par ^= 1u;
-        if (lane == 0) {
-          mbar_expect_tx(smem_addr(&ctl.q_full), kHeadsPerCta * row_bytes);
-          const int qrow = rv.token * args.num_heads + group * kHeadsPerCta;
-          for (int c = 0; c < nchunks; ++c)
-            tma_load_2d(sQ + c * kChunkBytes, &tm_q, c * 64, qrow, smem_addr(&ctl.q_full));
-        }
-        __syncwarp();
-      }
 
       // ---- key tiles ----
       const int act_q = args.q_len[rv.b];
@@ -602,119 +643,87 @@ __global__ void __launch_bounds__(kThreads, 1)
           m1mask = (uint64_t)__ballot_sync(0xffffffffu, ma) |
                    ((uint64_t)__ballot_sync(0xffffffffu, mb) << 32);
         }
-        // Slots resolved by this warp: LSU gather, keys 16 pw .. 16 pw + 15
-        // (lanes 16..31 mirror 0..15); TMA gather, all 64 keys (slot lane and
-        // slot lane + 32).
-        const int ka = lsu ? (pw * 16 + (lane & 15)) : lane;
-        const int kb = ka + 32;
+        // Slots resolved by this warp: keys 16 pw .. 16 pw + 15 (lanes 16..31
+        // mirror lanes 0..15).
+        const int ka = pw * 16 + (lane & 15);
         const bool blk_a = stopped || ((m1mask & ((1ull << ka) - 1ull)) != 0);
-        const bool blk_b = stopped || ((m1mask & ((1ull << (kb & 63)) - 1ull)) != 0);
         const SlotSrc sa = resolve_slot(args, rv, qk, j * kTileKeys + ka, idx_row, blk_a, err);
-        SlotSrc sb{-1, -1, false};
-        if (!lsu) sb = resolve_slot(args, rv, qk, j * kTileKeys + kb, idx_row, blk_b, err);
         if (m1mask != 0) stopped = true;
         const uint32_t va = __ballot_sync(0xffffffffu, sa.valid);
-        const uint32_t vb = __ballot_sync(0xffffffffu, sb.valid);
         if (leader && lane == 0) trace(tr, 0, 3 * produced);
         if (!__all_sync(0xffffffffu,
-                        wait_bar(&ctl, &ctl.kv_empty[stage], kv_empty_par[stage], err, 2))) {
+                        wait_bar(&ctl, &ctl.kv_empty[stage], (kv_empty_par >> stage) & 1u, err, 2))) {
           ok = false;
           break;
         }
         if (leader && lane == 0) trace(tr, 0, 3 * produced + 1);
-        kv_empty_par[stage] ^= 1u;
+        kv_empty_par ^= 1u << stage;
         const uint32_t bar = smem_addr(&ctl.kv_full[stage]);
         const uint32_t sK = sK0 + stage * kStageBytes;
+        if (lane == 0) ctl.valid[stage][pw] = (uint16_t)(va & 0xffffu);
         if (lsu) {
-          if (lane == 0) ctl.valid[stage][pw] = (uint16_t)(va & 0xffffu);
           __syncwarp();
           if (lane == 0) mbar_arrive(bar);
-          // 16 rows of this warp, 512 contiguous bytes per warp instruction;
-          // rows without a source are zero-filled (src size 0).
-          for (int k = 0; k < 16; ++k) {
-            const int row = __shfl_sync(0xffffffffu, sa.row, k);
-            const int pool = __shfl_sync(0xffffffffu, sa.pool, k);
-            const bool has = (pool >= 0 && row >= 0);
-            const char* src = reinterpret_cast<const char*>(pool == 1 ? args.cmp_kv : args.ori_kv);
-            if (has) src += (size_t)row * row_bytes;
-            else src = reinterpret_cast<const char*>(args.ori_kv);
-            const int key = pw * 16 + k;
-            for (int gi = lane; gi < gran; gi += 32)
-              cp_async_16(sK + (gi >> 3) * kChunkBytes + swz(key, gi & 7), src + gi * 16,
-                          has ? 16u : 0u);
-          }
-          cp_async_arrive_noinc(bar);
+          lsu_rows(args, sK, pw * 16, 0, 16, sa.row, sa.pool, lane, row_bytes, gran);
         } else {
-          if (lane == 0) {
-            ctl.valid[stage][0] = (uint16_t)(va & 0xffffu);
-            ctl.valid[stage][1] = (uint16_t)(va >> 16);
-            ctl.valid[stage][2] = (uint16_t)(vb & 0xffffu);
-            ctl.valid[stage][3] = (uint16_t)(vb >> 16);
-            mbar_expect_tx(bar, kTileKeys * row_bytes);
-          }
-          __syncwarp();
-          issue_tile<false>(&tm_ori, &tm_cmp, args.ori_rows, args.cmp_rows, nchunks, sK, bar,
-                            lane, sa.row, sa.pool, sb.row, sb.pool);
+          tma_rows(args, &tm_ori, &tm_cmp, nchunks, sK, bar, pw * 16, sa.row, sa.pool, lane,
+                   row_bytes, gran);
         }
+        cp_async_arrive_noinc(bar);
         if (leader && lane == 0) trace(tr, 0, 3 * produced + 2);
         ++produced;
         stage ^= 1;
       }
     }
-    if (lsu) cp_async_wait_all();
+    cp_async_wait_all();
+  } else if (warp == kQWarp) {
+    // ======================= Q loader =======================
+    // Q of a row (64 heads of this group, one 64 x 64 TMA box per chunk) is
+    // loaded once the last QK of the previous row has released the Q buffer;
+    // the next row's Q is prefetched into L2 meanwhile, so that wait is
+    // followed by an L2 read rather than an HBM one.
+    if (lane == 0) {
+      const uint32_t q_bytes = (uint32_t)kHeadsPerCta * (uint32_t)args.head_dim * 2u;
+      uint32_t q_empty_par = 1u;
+      int next = span.r0;  // first row whose Q has not been prefetched
+      auto qrow_of = [&](int r, int* qrow) -> bool {
+        const Row rv = load_row(rows, r);
+        const int tiles = row_tiles(rv);
+        const int ja = (r == span.r0) ? span.t0 : 0;
+        const int jb = (r == span.r1) ? span.t1 : (tiles > 0 ? tiles : 1);
+        *qrow = rv.token * args.num_heads + group * kHeadsPerCta;
+        return tiles > 0 && ja < jb;
+      };
+      for (int r = span.r0; span.r0 >= 0 && r <= span.r1; ++r) {
+        int qrow;
+        if (!qrow_of(r, &qrow)) continue;
+        // L2 prefetch of the next row that has key tiles.
+        for (next = max(next, r + 1); next <= span.r1; ++next) {
+          int nq;
+          if (qrow_of(next, &nq)) {
+            for (int c = 0; c < nchunks; ++c) tma_prefetch_2d(&tm_q, c * 64, nq);
+            ++next;
+            break;
+          }
+        }
+        if (!wait_bar(&ctl, &ctl.q_empty, q_empty_par, err, 1)) break;
+        q_empty_par ^= 1u;
+        mbar_expect_tx(smem_addr(&ctl.q_full), q_bytes);
+        for (int c = 0; c < nchunks; ++c)
+          tma_load_2d(sQ + c * kChunkBytes, &tm_q, c * 64, qrow, smem_addr(&ctl.q_full));
+      }
+    }
+    __syncwarp();
   } else if (warp == kMmaWarp) {
     // ======================= MMA issuer =======================
     if (lane == 0) {
       const uint32_t idesc_qk = instr_desc(64, 64, kBf16, false, false);
       const uint32_t idesc_pv = instr_desc(64, 256, kBf16, false, true);
-      uint32_t kv_full_par[2] = {0u, 0u};
-      uint32_t s_empty_par[2] = {1u, 1u};
+      // Barrier parities as bits: kv_full (bit = stage), s_empty (bit = S buffer).
+      uint32_t kv_full_par = 0u, s_empty_par = 3u;
       uint32_t q_full_par = 0u, p_full_par = 0u, o_free_par = 1u;
-      int stage = 0, sbuf = 0, pv_issued = 0;
+      int stage = 0, sbuf = 0, pv_issued = 0, qk_issued = 0;
       bool ok = true;
-
-      // QK(j) into S buffer sb from K stage st (inputs already acquired).
-      int qk_issued = 0;
-      auto qk = [&](int st, int sb) {
-        trace(tr, 1, 2 * qk_issued);
-        ++qk_issued;
-        fence_proxy_async();
-        tc_fence_after();
-        // Chunk c accumulates into partial c % 4; consecutive MMAs rotate
-        // over the partials so four dependent chains overlap in the pipe.
-        const uint32_t d = tmem + kTmemS + 128u * sb;
-        const uint32_t kb = sK0 + st * kStageBytes;
-        for (int c4 = 0; c4 < nchunks; c4 += kQkPartials) {
-          for (int ks = 0; ks < 4; ++ks) {
-            for (int pp = 0; pp < kQkPartials; ++pp) {
-              const int c = c4 + pp;
-              if (c >= nchunks) break;
-              const uint64_t a = smem_desc(sQ + c * kChunkBytes + ks * 32, 16, 1024);
-              const uint64_t b = smem_desc(kb + c * kChunkBytes + ks * 32, 16, 1024);
-              mma_ws(d + 32u * pp, a, b, idesc_qk, (c4 == 0 && ks == 0) ? 0u : 1u);
-            }
-          }
-        }
-        tc_commit(smem_addr(&ctl.s_full[sb]));
-      };
-      // O (+)= P V for the tile in K stage st.
-      auto pv = [&](int st, bool first) {
-        trace(tr, 1, 2 * pv_issued + 1);
-        fence_proxy_async();
-        tc_fence_after();
-        const uint32_t kb = sK0 + st * kStageBytes;
-        for (int ks = 0; ks < 4; ++ks) {
-          const uint64_t a = smem_desc(kb + kPChunk * kChunkBytes + ks * 32, 16, 1024);
-          for (int hv = 0; hv < 2; ++hv) {
-            const uint64_t b =
-                smem_desc(kb + (4 * hv) * kChunkBytes + ks * 2048, kChunkBytes, 1024);
-            mma_ws(tmem + kTmemO + 128u * hv, a, b, idesc_pv, (first && ks == 0) ? 0u : 1u);
-          }
-        }
-        tc_commit(smem_addr(&ctl.kv_empty[st]));
-        tc_commit(smem_addr(&ctl.pv_done[pv_issued & 1]));
-        ++pv_issued;
-      };
 
       for (int r = span.r0; ok && span.r0 >= 0 && r <= span.r1; ++r) {
         const Row rv = load_row(rows, r);
@@ -724,11 +733,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (tiles == 0 || ja >= jb) continue;
         if (!wait_bar(&ctl, &ctl.q_full, q_full_par, err, 22)) { ok = false; break; }
         q_full_par ^= 1u;
-        if (!wait_bar(&ctl, &ctl.kv_full[stage], kv_full_par[stage], err, 20)) { ok = false; break; }
-        kv_full_par[stage] ^= 1u;
-        if (!wait_bar(&ctl, &ctl.s_empty[sbuf], s_empty_par[sbuf], err, 21)) { ok = false; break; }
-        s_empty_par[sbuf] ^= 1u;
-        qk(stage, sbuf);
+        if (!wait_bar(&ctl, &ctl.kv_full[stage], (kv_full_par >> stage) & 1u, err, 20)) { ok = false; break; }
+        kv_full_par ^= 1u << stage;
+        if (!wait_bar(&ctl, &ctl.s_empty[sbuf], (s_empty_par >> sbuf) & 1u, err, 21)) { ok = false; break; }
+        s_empty_par ^= 1u << sbuf;
+        fence_proxy_async();
+        tc_fence_after();
+        trace(tr, 1, 4 * qk_issued);
+        issue_qk<nchunks>(tmem + kTmemS + 128u * sbuf, sQ, sK0 + stage * kStageBytes, idesc_qk);
+        trace(tr, 1, 4 * qk_issued + 1);
+        ++qk_issued;
+        tc_commit(smem_addr(&ctl.s_full[sbuf]));
         if (jb - ja == 1) tc_commit(smem_addr(&ctl.q_empty));
         for (int j = ja; j < jb && ok; ++j) {
           const int st = stage;
@@ -742,16 +757,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           while (need_qk || need_pv) {
             bool progress = false;
             if (need_qk) {
-              if (!kv_ok && mbar_test(smem_addr(&ctl.kv_full[stage]), kv_full_par[stage])) {
+              if (!kv_ok && mbar_test(smem_addr(&ctl.kv_full[stage]), (kv_full_par >> stage) & 1u)) {
                 kv_ok = true;
-                kv_full_par[stage] ^= 1u;
+                kv_full_par ^= 1u << stage;
               }
-              if (!s_ok && mbar_test(smem_addr(&ctl.s_empty[sbuf]), s_empty_par[sbuf])) {
+              if (!s_ok && mbar_test(smem_addr(&ctl.s_empty[sbuf]), (s_empty_par >> sbuf) & 1u)) {
                 s_ok = true;
-                s_empty_par[sbuf] ^= 1u;
+                s_empty_par ^= 1u << sbuf;
               }
               if (kv_ok && s_ok) {
-                qk(stage, sbuf);
+                fence_proxy_async();
+                tc_fence_after();
+                trace(tr, 1, 4 * qk_issued);
+                issue_qk<nchunks>(tmem + kTmemS + 128u * sbuf, sQ, sK0 + stage * kStageBytes,
+                                  idesc_qk);
+                trace(tr, 1, 4 * qk_issued + 1);
+                ++qk_issued;
+                tc_commit(smem_addr(&ctl.s_full[sbuf]));
                 if (j + 2 == jb) tc_commit(smem_addr(&ctl.q_empty));
                 need_qk = false;
                 progress = true;
@@ -767,7 +789,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 o_free_par ^= 1u;
               }
               if (p_ok && o_ok) {
-                pv(st, j == ja);
+                trace(tr, 1, 4 * pv_issued + 2);
+                fence_proxy_async();
+                tc_fence_after();
+                issue_pv(tmem + kTmemO, sK0 + st * kStageBytes, idesc_pv, j == ja);
+                trace(tr, 1, 4 * pv_issued + 3);
+                tc_commit(smem_addr(&ctl.kv_empty[st]));
+                tc_commit(smem_addr(&ctl.pv_done[pv_issued & 1]));
+                ++pv_issued;
                 need_pv = false;
                 progress = true;
               }
@@ -800,8 +829,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     const float c2 = args.softmax_scale * kLog2e;
     const float sink = live ? __ldg(args.sinks + head) : -INFINITY;
-    uint32_t kv_full_par[2] = {0u, 0u};
-    uint32_t s_full_par[2] = {0u, 0u};
+    uint32_t kv_full_par = 0u, s_full_par = 0u;  // bit = stage / S buffer
     int pv_count = 0;  // PVs released by this thread's p_full arrivals so far
     int rows_done = 0;
     // Completion of PV number k: phase k/2 of pv_done[k % 2].  When softmax
@@ -813,14 +841,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto wait_pv = [&](int k, int site) -> bool {
       return wait_bar(&ctl, &ctl.pv_done[k & 1], (uint32_t)((k >> 1) & 1), err, site);
     };
-    uint32_t xph[2] = {0u, 0u};
+    uint32_t xph = 0u;  // bit = exchange barrier
     int stage = 0, sbuf = 0, xpar = 0;
     // Partner exchange through ctl.red[xpar], ordered by the bounded
     // mbarrier ctl.xbar[xpar] (all 128 softmax threads arrive, then wait).
     auto exchange = [&](int site) -> bool {
       mbar_arrive(smem_addr(&ctl.xbar[xpar]));
-      const bool w = wait_bar(&ctl, &ctl.xbar[xpar], xph[xpar], err, site);
-      xph[xpar] ^= 1u;
+      const bool w = wait_bar(&ctl, &ctl.xbar[xpar], (xph >> xpar) & 1u, err, site);
+      xph ^= 1u << xpar;
       return w;
     };
     bool ok = true;
@@ -850,10 +878,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int st = stage, sb = sbuf;
         stage ^= 1;
         sbuf ^= 1;
-        if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.s_full[sb], s_full_par[sb], err, 30))) { ok = false; break; }
-        s_full_par[sb] ^= 1u;
-        if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.kv_full[st], kv_full_par[st], err, 31))) { ok = false; break; }
-        kv_full_par[st] ^= 1u;
+        if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.s_full[sb], (s_full_par >> sb) & 1u, err, 30))) { ok = false; break; }
+        s_full_par ^= 1u << sb;
+        if (threadIdx.x == 0) trace(tr, 2, 4 * pv_count + 3);
+        if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.kv_full[st], (kv_full_par >> st) & 1u, err, 31))) { ok = false; break; }
+        kv_full_par ^= 1u << st;
         if (threadIdx.x == 0) trace(tr, 2, 4 * pv_count);
         tc_fence_after();
         uint32_t sraw[32];
@@ -1047,16 +1076,25 @@ static bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t c
   return r == CUDA_SUCCESS;
 }
 
-int launch_fwd(const FwdArgs& args, int grid, cudaStream_t stream) {
-  static bool configured[2] = {false, false};
-  const bool bf16 = args.dtype == SAS_DTYPE_BF16;
-  const void* fn = bf16 ? (const void*)sas_fwd_kernel<true> : (const void*)sas_fwd_kernel<false>;
-  if (!configured[bf16 ? 0 : 1]) {
-    cudaError_t e =
-        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemDynamic);
-    if (e != cudaSuccess) return SAS_ERR_CUDA;
-    configured[bf16 ? 0 : 1] = true;
+template <bool kBf16, int kChunks>
+static int launch_one(const FwdArgs& args, int grid, cudaStream_t stream, const CUtensorMap& tm_q,
+                      const CUtensorMap& tm_ori, const CUtensorMap& tm_cmp) {
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(sas_fwd_kernel<kBf16, kChunks>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSmemDynamic) != cudaSuccess)
+      return SAS_ERR_CUDA;
+    configured = true;
   }
+  sas_fwd_kernel<kBf16, kChunks><<<grid, kThreads, kSmemDynamic, stream>>>(args, tm_q, tm_ori,
+                                                                           tm_cmp);
+  return cudaGetLastError() == cudaSuccess ? SAS_OK : SAS_ERR_CUDA;
+}
+
+int launch_fwd(const FwdArgs& args, int grid, cudaStream_t stream) {
+  const bool bf16 = args.dtype == SAS_DTYPE_BF16;
+  if (args.head_dim != 576 && args.head_dim != 512) return SAS_ERR_UNSUPPORTED;
   alignas(64) CUtensorMap tm_q, tm_ori, tm_cmp;
   const uint64_t D = (uint64_t)args.head_dim;
   if (!make_map(&tm_q, args.q, (uint64_t)args.total_tokens * args.num_heads, D, kHeadsPerCta))
@@ -1067,11 +1105,11 @@ int launch_fwd(const FwdArgs& args, int grid, cudaStream_t stream) {
   } else {
     tm_cmp = tm_ori;
   }
-  if (bf16)
-    sas_fwd_kernel<true><<<grid, kThreads, kSmemDynamic, stream>>>(args, tm_q, tm_ori, tm_cmp);
-  else
-    sas_fwd_kernel<false><<<grid, kThreads, kSmemDynamic, stream>>>(args, tm_q, tm_ori, tm_cmp);
-  return cudaGetLastError() == cudaSuccess ? SAS_OK : SAS_ERR_CUDA;
+  if (args.head_dim == 576)
+    return bf16 ? launch_one<true, 9>(args, grid, stream, tm_q, tm_ori, tm_cmp)
+                : launch_one<false, 9>(args, grid, stream, tm_q, tm_ori, tm_cmp);
+  return bf16 ? launch_one<true, 8>(args, grid, stream, tm_q, tm_ori, tm_cmp)
+              : launch_one<false, 8>(args, grid, stream, tm_q, tm_ori, tm_cmp);
 }
 
 }  // namespace sas

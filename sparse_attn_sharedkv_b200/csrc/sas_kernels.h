@@ -36,7 +36,7 @@ struct FwdArgs {
   int32_t total_tokens;     // rows of q (for the Q tensor map)
   int32_t ori_rows;         // ori_num_blocks * ori_block_size (out-of-range row = zero fill)
   int32_t cmp_rows;         // cmp_num_blocks * cmp_block_size
-  int32_t gather;           // key-row gather: 0 = cp.async (LSU), 1 = TMA gather4
+  int32_t gather;           // key-row gather: 0 = cp.async (LSU), 1 = TMA gather4 (default)
 };
 
 int launch_fwd(const FwdArgs& args, int grid, cudaStream_t stream);
