@@ -287,6 +287,9 @@ struct Ctl {
   volatile int abort;
   uint16_t valid[2][4];          // per stage: slot bits of keys 16w..16w+15
   float red[2][2][kHeadsPerCta];  // [parity][half][row]: partner exchange
+  // Epilogue staging: per softmax warp, 32 head rows x 64 bytes, so each
+  // global store instruction writes whole 64-byte row segments.
+  alignas(128) uint8_t epi[kNumSoftmaxWarps][32 * 64];
 };
 
 struct Row {
@@ -476,6 +479,28 @@ __device__ __forceinline__ void tma_rows(const FwdArgs& a, const CUtensorMap* tm
     lsu_rows(a, sK, key0, 4 * (__ffs(mm) - 1), 4, r, p, lane, row_bytes, gran);
 }
 
+// Coalesced store of one softmax warp's 32 rows x 64 bytes: lane i holds
+// row i's 64 bytes in v[0..3] (row i = head m0 + i).  The rows go through
+// the warp's 2 KB staging buffer (16-byte slot q of row i at slot
+// q ^ ((i >> 1) & 3): conflict-free both ways) and come back out as eight
+// whole rows per store instruction (lane j: row 8 s + j / 4, slot j % 4).
+// Rows at or past `nlive` (heads >= H) are not written.
+__device__ __forceinline__ void warp_store_rows64(uint8_t* stg, int lane, const uint4 (&v)[4],
+                                                  char* seg0, size_t stride, int nlive) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    *reinterpret_cast<uint4*>(stg + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) = v[q];
+  __syncwarp();
+  const int u = lane & 3;
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    const int hl = 8 * s + (lane >> 2);
+    const uint4 w = *reinterpret_cast<const uint4*>(stg + hl * 64 + ((u ^ ((hl >> 1) & 3)) << 4));
+    if (hl < nlive) *reinterpret_cast<uint4*>(seg0 + (size_t)hl * stride + u * 16) = w;
+  }
+  __syncwarp();
+}
+
 // S[sb] = Q K^T for the K tile at kb: chunk c accumulates into partial c % 4
 // and consecutive MMAs rotate over the partials, so four dependent chains
 // overlap in the pipe.  Descriptors are built once and advanced by constant
@@ -535,7 +560,9 @@ template <bool kBf16, int kChunks>
 __global__ void __launch_bounds__(kThreads, 1)
     sas_fwd_kernel(const FwdArgs args, const __grid_constant__ CUtensorMap tm_q,
                    const __grid_constant__ CUtensorMap tm_ori,
-                   const __grid_constant__ CUtensorMap tm_cmp) {
+                   const __grid_constant__ CUtensorMap tm_cmp,
+                   const __grid_constant__ CUtensorMap tm_ori16,
+                   const __grid_constant__ CUtensorMap tm_cmp16) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ Ctl ctl;
 
@@ -666,8 +693,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) mbar_arrive(bar);
           lsu_rows(args, sK, pw * 16, 0, 16, sa.row, sa.pool, lane, row_bytes, gran);
         } else {
-          tma_rows(args, &tm_ori, &tm_cmp, nchunks, sK, bar, pw * 16, sa.row, sa.pool, lane,
-                   row_bytes, gran);
+          // The warp's 16 slots read 16 consecutive rows of one cache (window
+          // keys inside one page, contiguous compressed positions): one
+          // 16-row TMA box per chunk instead of four gather4 ops.
+          const int row0 = __shfl_sync(0xffffffffu, sa.row, 0);
+          const int pool0 = __shfl_sync(0xffffffffu, sa.pool, 0);
+          const bool run16 = __all_sync(0xffffffffu, pool0 >= 0 && sa.pool == pool0 &&
+                                                         sa.row >= 0 &&
+                                                         sa.row == row0 + (lane & 15));
+          if (run16) {
+            if (lane == 0) {
+              mbar_expect_tx(bar, 16u * row_bytes);
+              const CUtensorMap* m = (pool0 == 1) ? &tm_cmp16 : &tm_ori16;
+              const uint32_t dst = sK + (uint32_t)(pw * 16) * 128u;
+#pragma unroll
+              for (int c = 0; c < nchunks; ++c)
+                tma_load_2d(dst + c * kChunkBytes, m, c * 64, row0, bar);
+            }
+          } else {
+            tma_rows(args, &tm_ori, &tm_cmp, nchunks, sK, bar, pw * 16, sa.row, sa.pool, lane,
+                     row_bytes, gran);
+          }
         }
         cp_async_arrive_noinc(bar);
         if (leader && lane == 0) trace(tr, 0, 3 * produced + 2);
@@ -685,6 +731,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t q_bytes = (uint32_t)kHeadsPerCta * (uint32_t)args.head_dim * 2u;
       uint32_t q_empty_par = 1u;
+      int q_loads = 0;
       int next = span.r0;  // first row whose Q has not been prefetched
       auto qrow_of = [&](int r, int* qrow) -> bool {
         const Row rv = load_row(rows, r);
@@ -708,6 +755,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!wait_bar(&ctl, &ctl.q_empty, q_empty_par, err, 1)) break;
         q_empty_par ^= 1u;
+        trace(tr, 3, 4096 + q_loads++);
         mbar_expect_tx(smem_addr(&ctl.q_full), q_bytes);
         for (int c = 0; c < nchunks; ++c)
           tma_load_2d(sQ + c * kChunkBytes, &tm_q, c * 64, qrow, smem_addr(&ctl.q_full));
@@ -722,7 +770,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Barrier parities as bits: kv_full (bit = stage), s_empty (bit = S buffer).
       uint32_t kv_full_par = 0u, s_empty_par = 3u;
       uint32_t q_full_par = 0u, p_full_par = 0u, o_free_par = 1u;
-      int stage = 0, sbuf = 0, pv_issued = 0, qk_issued = 0;
+      int stage = 0, sbuf = 0, pv_issued = 0, qk_issued = 0, q_seen = 0;
       bool ok = true;
 
       for (int r = span.r0; ok && span.r0 >= 0 && r <= span.r1; ++r) {
@@ -733,6 +781,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (tiles == 0 || ja >= jb) continue;
         if (!wait_bar(&ctl, &ctl.q_full, q_full_par, err, 22)) { ok = false; break; }
         q_full_par ^= 1u;
+        trace(tr, 3, 6144 + q_seen++);
         if (!wait_bar(&ctl, &ctl.kv_full[stage], (kv_full_par >> stage) & 1u, err, 20)) { ok = false; break; }
         kv_full_par ^= 1u << stage;
         if (!wait_bar(&ctl, &ctl.s_empty[sbuf], (s_empty_par >> sbuf) & 1u, err, 21)) { ok = false; break; }
@@ -976,13 +1025,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       // ---- epilogue of this (row, piece) ----
-      if (threadIdx.x == 0) trace(tr, 3, 2 * rows_done);
+      if (threadIdx.x == 0) trace(tr, 3, 3 * rows_done);
       if (!__all_sync(0xffffffffu, wait_pv(pv_count - 1, 33))) {
         ok = false;
         break;
       }
-      if (threadIdx.x == 0) trace(tr, 3, 2 * rows_done + 1);
-      ++rows_done;
+      if (threadIdx.x == 0) trace(tr, 3, 3 * rows_done + 1);
       tc_fence_after();
       ctl.red[xpar][half][m] = l_run;
       if (!__all_sync(0xffffffffu, exchange(35))) { ok = false; break; }
@@ -991,38 +1039,53 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool split = rv.partial_base >= 0;
       const float inv = (l_tot > 0.f) ? 1.f / l_tot : 0.f;
       const float lse = (m_run + log2f(l_tot)) * kLn2;
+      // Heads of this warp: group * 64 + m0 + i, i = lane (m0 = 0 or 32).
+      const int m0 = (warp & 1) * 32;
+      const int nlive = min(32, max(0, args.num_heads - (group * kHeadsPerCta + m0)));
+      const size_t row0 = (size_t)rv.token * args.num_heads + group * kHeadsPerCta + m0;
+      const int piece = (r == span.r0) ? span.piece0 : 0;
+      const size_t prow0 =
+          split ? (size_t)(rv.partial_base + piece) * args.num_heads + group * kHeadsPerCta + m0
+                : 0;
+      uint8_t* stg = ctl.epi[warp];
       for (int c = 0; c < 8; ++c) {
         uint32_t v[32];
         tmem_ld32(tmem + lane_off + kTmemO + 32u * c, v);
         tmem_wait_ld();
-        if (!live) continue;
         // Column block c: accumulator hv = c / 4, dims hv*256 + half*128 + (c%4)*32.
         const int d0 = (c >> 2) * 256 + half * 128 + (c & 3) * 32;
         if (split) {
-          const int piece = (r == span.r0) ? span.piece0 : 0;
-          float* o = args.o_partial +
-                     ((size_t)(rv.partial_base + piece) * args.num_heads + head) * dv + d0;
 #pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            *reinterpret_cast<float4*>(o + i) =
-                make_float4(__uint_as_float(v[i]) * inv, __uint_as_float(v[i + 1]) * inv,
-                            __uint_as_float(v[i + 2]) * inv, __uint_as_float(v[i + 3]) * inv);
+          for (int hh = 0; hh < 2; ++hh) {
+            uint4 w[4];
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              const int i = 16 * hh + 4 * g;
+              w[g] = make_uint4(__float_as_uint(__uint_as_float(v[i]) * inv),
+                                __float_as_uint(__uint_as_float(v[i + 1]) * inv),
+                                __float_as_uint(__uint_as_float(v[i + 2]) * inv),
+                                __float_as_uint(__uint_as_float(v[i + 3]) * inv));
+            }
+            char* seg0 = reinterpret_cast<char*>(args.o_partial + prow0 * dv + d0 + 16 * hh);
+            warp_store_rows64(stg, lane, w, seg0, (size_t)dv * 4, nlive);
           }
         } else {
-          uint32_t pkd[16];
+          uint4 w[4];
 #pragma unroll
-          for (int i = 0; i < 32; i += 2)
-            pkd[i / 2] = pack2<kBf16>(__uint_as_float(v[i]) * inv, __uint_as_float(v[i + 1]) * inv);
-          uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<char*>(args.out) +
-                                              (orow * dv + d0) * 2);
-#pragma unroll
-          for (int g = 0; g < 4; ++g)
-            o[g] = make_uint4(pkd[4 * g], pkd[4 * g + 1], pkd[4 * g + 2], pkd[4 * g + 3]);
+          for (int g = 0; g < 4; ++g) {
+            const int i = 8 * g;
+            w[g] = make_uint4(
+                pack2<kBf16>(__uint_as_float(v[i]) * inv, __uint_as_float(v[i + 1]) * inv),
+                pack2<kBf16>(__uint_as_float(v[i + 2]) * inv, __uint_as_float(v[i + 3]) * inv),
+                pack2<kBf16>(__uint_as_float(v[i + 4]) * inv, __uint_as_float(v[i + 5]) * inv),
+                pack2<kBf16>(__uint_as_float(v[i + 6]) * inv, __uint_as_float(v[i + 7]) * inv));
+          }
+          char* seg0 = reinterpret_cast<char*>(args.out) + (row0 * dv + d0) * 2;
+          warp_store_rows64(stg, lane, w, seg0, (size_t)dv * 2, nlive);
         }
       }
       if (live && half == 0) {
         if (split) {
-          const int piece = (r == span.r0) ? span.piece0 : 0;
           args.lse_partial[(size_t)(rv.partial_base + piece) * args.num_heads + head] = lse;
         } else {
           args.lse[orow] = lse;
@@ -1030,6 +1093,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(smem_addr(&ctl.o_free));
+      if (threadIdx.x == 0) trace(tr, 3, 3 * rows_done + 2);
+      ++rows_done;
     }
   }
 
@@ -1078,7 +1143,8 @@ static bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t c
 
 template <bool kBf16, int kChunks>
 static int launch_one(const FwdArgs& args, int grid, cudaStream_t stream, const CUtensorMap& tm_q,
-                      const CUtensorMap& tm_ori, const CUtensorMap& tm_cmp) {
+                      const CUtensorMap& tm_ori, const CUtensorMap& tm_cmp,
+                      const CUtensorMap& tm_ori16, const CUtensorMap& tm_cmp16) {
   static bool configured = false;
   if (!configured) {
     if (cudaFuncSetAttribute(sas_fwd_kernel<kBf16, kChunks>,
@@ -1087,29 +1153,39 @@ static int launch_one(const FwdArgs& args, int grid, cudaStream_t stream, const 
       return SAS_ERR_CUDA;
     configured = true;
   }
-  sas_fwd_kernel<kBf16, kChunks><<<grid, kThreads, kSmemDynamic, stream>>>(args, tm_q, tm_ori,
-                                                                           tm_cmp);
+  sas_fwd_kernel<kBf16, kChunks><<<grid, kThreads, kSmemDynamic, stream>>>(
+      args, tm_q, tm_ori, tm_cmp, tm_ori16, tm_cmp16);
   return cudaGetLastError() == cudaSuccess ? SAS_OK : SAS_ERR_CUDA;
 }
 
 int launch_fwd(const FwdArgs& args, int grid, cudaStream_t stream) {
   const bool bf16 = args.dtype == SAS_DTYPE_BF16;
   if (args.head_dim != 576 && args.head_dim != 512) return SAS_ERR_UNSUPPORTED;
-  alignas(64) CUtensorMap tm_q, tm_ori, tm_cmp;
+  // Key-cache maps: one-row boxes (gather4 and single rows) and 16-row
+  // boxes (runs of 16 consecutive rows).
+  alignas(64) CUtensorMap tm_q, tm_ori, tm_cmp, tm_ori16, tm_cmp16;
   const uint64_t D = (uint64_t)args.head_dim;
   if (!make_map(&tm_q, args.q, (uint64_t)args.total_tokens * args.num_heads, D, kHeadsPerCta))
     return SAS_ERR_CUDA;
   if (!make_map(&tm_ori, args.ori_kv, (uint64_t)args.ori_rows, D, 1)) return SAS_ERR_CUDA;
+  // A cache with fewer than 16 rows never takes the 16-row run path, so its
+  // 16-row map is encoded with a box that fits the cache.
+  const uint32_t ori_box = args.ori_rows < 16 ? (uint32_t)args.ori_rows : 16u;
+  const uint32_t cmp_box = args.cmp_rows < 16 ? (uint32_t)args.cmp_rows : 16u;
+  if (!make_map(&tm_ori16, args.ori_kv, (uint64_t)args.ori_rows, D, ori_box)) return SAS_ERR_CUDA;
   if (args.cmp_kv != nullptr && args.cmp_rows > 0) {
     if (!make_map(&tm_cmp, args.cmp_kv, (uint64_t)args.cmp_rows, D, 1)) return SAS_ERR_CUDA;
+    if (!make_map(&tm_cmp16, args.cmp_kv, (uint64_t)args.cmp_rows, D, cmp_box)) return SAS_ERR_CUDA;
   } else {
     tm_cmp = tm_ori;
+    tm_cmp16 = tm_ori16;
   }
   if (args.head_dim == 576)
-    return bf16 ? launch_one<true, 9>(args, grid, stream, tm_q, tm_ori, tm_cmp)
-                : launch_one<false, 9>(args, grid, stream, tm_q, tm_ori, tm_cmp);
-  return bf16 ? launch_one<true, 8>(args, grid, stream, tm_q, tm_ori, tm_cmp)
-              : launch_one<false, 8>(args, grid, stream, tm_q, tm_ori, tm_cmp);
+    return bf16 ? launch_one<true, 9>(args, grid, stream, tm_q, tm_ori, tm_cmp, tm_ori16, tm_cmp16)
+                : launch_one<false, 9>(args, grid, stream, tm_q, tm_ori, tm_cmp, tm_ori16,
+                                       tm_cmp16);
+  return bf16 ? launch_one<true, 8>(args, grid, stream, tm_q, tm_ori, tm_cmp, tm_ori16, tm_cmp16)
+              : launch_one<false, 8>(args, grid, stream, tm_q, tm_ori, tm_cmp, tm_ori16, tm_cmp16);
 }
 
 }  // namespace sas
