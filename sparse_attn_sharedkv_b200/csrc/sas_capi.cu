@@ -136,6 +136,11 @@ extern "C" int sas_fwd_execute(const SasProblem* prob, const SasFwdParams* param
   a.lse = f.lse;
   a.err = f.err;
   a.trace = reinterpret_cast<long long*>(f.trace);
+  a.trace_cta = 0;
+  if (f.trace != nullptr) {
+    const char* e = getenv("SAS_TRACE_CTA");
+    a.trace_cta = e != nullptr ? atoi(e) : 0;
+  }
   a.plan = dplan;
   a.q_len = dplan + info.actq_off;
   a.kv_len = dplan + info.actkv_off;

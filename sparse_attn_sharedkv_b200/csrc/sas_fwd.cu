@@ -7,24 +7,28 @@
 // every key row is an L2 hit.
 //
 // Per tile of 64 key slots (window keys then compressed keys, golden.py
-// tile order) the CTA runs:
+// tile order), 16 warps in five roles:
 //
-//   producer warps (4)  slot -> (cache, logical pos) -> block table -> row
-//                       for 16 keys each; TMA tile::gather4 of 4 rows x 128 B
-//                       per op into a 128B-swizzled K tile, issued from all
-//                       four warps (TMA issue is per-warp serial, so four
-//                       issuing warps move ~2.7x the bytes of one) (paged
-//                       window load, kernel.py:3580-3600, and top-k gather,
-//                       kernel.py:2606-2751); -1 stop / threshold masks
-//                       (golden.py:28-66) into a per-tile valid mask; Q tiles
-//                       by 64 x 64 TMA boxes
-//   MMA warp (1 lane)   S = Q K^T  : 36 x tcgen05.mma.ws M64 N64 K16 (d_qk 576)
+//   producer warps 4-7  slot -> (cache, logical pos) -> block table -> row
+//                       for 16 keys each (paged window load, kernel.py:
+//                       3580-3600, top-k gather, kernel.py:2606-2751, -1 stop
+//                       and threshold masks, golden.py:28-66) into a per-tile
+//                       valid mask; 16 consecutive rows of one cache move as
+//                       one 16-row TMA box per 64-column chunk, other rows by
+//                       TMA tile::gather4 (4 rows x 128 B per op) into the
+//                       128B-swizzled K tile
+//   Q warp 9            Q tile (64 heads) by 64 x 64 TMA boxes, next row's Q
+//                       prefetched into L2
+//   MMA warp 8 (1 lane) S = Q K^T  : 36 x tcgen05.mma.ws M64 N64 K16 (d_qk 576)
 //                       O += P V   : 8 x tcgen05.mma.ws M64 N256 K16, where V is
 //                                    the same smem K tile read MN-major (d_v 512)
-//   softmax warps (4)   tcgen05.ld of S, mask, scale, online softmax seeded
+//   softmax warps 0-3   tcgen05.ld of S, mask, scale, online softmax seeded
 //                       by the sink (golden.py:156-196) in the exp2 domain,
 //                       P rounded to the input dtype into smem, lazy O
-//                       rescale in TMEM, final O / l and LSE (kernel.py:3110-3245)
+//                       rescale in TMEM; hands m and l of each (row, piece) on
+//   epilogue warps 12-15 O / l -> out (or fp32 split partials) and the LSE
+//                       (kernel.py:3110-3245) through coalescing staging, then
+//                       release O to the next row, overlapping its QK/softmax
 //
 // TMEM (512 columns): O[64 x 512] fp32 as two .ws M64 N256 accumulators
 // (cols 0-255, all 128 lanes); S[64 x 64] fp32 double-buffered, each buffer
@@ -32,6 +36,7 @@
 // 36 small QK MMAs form four independent accumulation chains.
 // Shared memory: Q 72 KB and two K stages of 72 KB; P of a tile is written
 // into its stage's rope chunk (dims 512..575), which PV does not read.
+// 512 threads at 128 registers: every role fits without spills.
 //
 // Every wait on an mbarrier is bounded: on timeout the thread records an
 // error in the caller's error word, raises the CTA abort flag and leaves its
@@ -56,9 +61,13 @@ constexpr int kProducerWarp0 = 4;  // producer warps 4..7 gather key rows
 constexpr int kNumProducerWarps = 4;
 constexpr int kMmaWarp = 8;
 constexpr int kQWarp = 9;          // loads Q tiles by TMA, prefetches the next row's Q into L2
-constexpr int kThreads = 32 * 10;
+constexpr int kEpiWarp0 = 12;      // epilogue warps 12..15 (TMEM lane quarters 0..3)
+constexpr int kNumEpiWarps = 4;
+constexpr int kThreads = 32 * 16;  // warps 10, 11 have no role
+constexpr int kEpiThreads = 32 * kNumEpiWarps;
 constexpr int kSoftmaxThreads = 32 * kNumSoftmaxWarps;
 constexpr int kProducerThreads = 32 * kNumProducerWarps;
+
 constexpr int kQkPartials = 4;     // independent S accumulators per tile (QK chains)
 
 constexpr int kMaxChunks = 9;                   // d_qk / 64
@@ -229,6 +238,18 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "memory");
 }
 
+// 16 consecutive 32-bit columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
@@ -287,26 +308,49 @@ struct Ctl {
   volatile int abort;
   uint16_t valid[2][4];          // per stage: slot bits of keys 16w..16w+15
   float red[2][2][kHeadsPerCta];  // [parity][half][row]: partner exchange
-  // Epilogue staging: per softmax warp, 32 head rows x 64 bytes, so each
-  // global store instruction writes whole 64-byte row segments.
-  alignas(128) uint8_t epi[kNumSoftmaxWarps][32 * 64];
+  // Final statistics of a (row, piece), softmax -> epilogue warps, double-
+  // buffered by the parity of the piece's ordinal (the epilogue of piece k
+  // releases o_free before any PV, hence any QK, of piece k + 2 can start).
+  uint64_t fin_full[2];
+  uint64_t o_full;                  // O of a (row, piece) complete (last PV committed)
+  float fin_m[2][kHeadsPerCta];     // running max (log2 domain)
+  float fin_l[2][2][kHeadsPerCta];  // [parity][half][head] partial row sums
+  // Epilogue staging: per epilogue warp, 32 head rows x 32 bytes, so each
+  // global store instruction writes whole 32-byte sectors of 16 rows.
+  alignas(128) uint8_t epi[kNumEpiWarps][32 * 32];
 };
 
 struct Row {
-  int token, b, s, slots, flags, first_worker, partial_base, window;
+  int token, b, s, slots, flags, first_worker, partial_base, window, win_lo, cmp, thr;
 };
 
 __device__ __forceinline__ Row load_row(const int* rows, int r) {
   const int4* p = reinterpret_cast<const int4*>(rows + (size_t)r * kRowInts);
-  int4 a = __ldg(p), c = __ldg(p + 1);
-  return Row{a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+  int4 a = __ldg(p), c = __ldg(p + 1), e = __ldg(p + 2);
+  return Row{a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w, e.x, e.y, e.z};
 }
+
+// Plan rows of a worker span, each fetched one row ahead of its use so the
+// global-load latency overlaps the previous row's work.
+struct RowStream {
+  const int* rows;
+  int r1;
+  Row next;
+  __device__ __forceinline__ RowStream(const int* rows_, int r0, int r1_) : rows(rows_), r1(r1_) {
+    if (r0 >= 0 && r0 <= r1) next = load_row(rows, r0);
+  }
+  __device__ __forceinline__ Row take(int r) {
+    const Row cur = next;
+    if (r + 1 <= r1) next = load_row(rows, r + 1);
+    return cur;
+  }
+};
 
 // Diagnostic clock trace of CTA 0: 4 regions of 8192 entries (producer, MMA,
 // softmax per tile, epilogue per row).
 constexpr int kTraceRegion = 8192;
 __device__ __forceinline__ void trace(long long* tr, int region, int idx) {
-  if (tr != nullptr && blockIdx.x == 0 && idx >= 0 && idx < kTraceRegion)
+  if (tr != nullptr && idx >= 0 && idx < kTraceRegion)
     tr[region * kTraceRegion + idx] = clock64();
 }
 
@@ -479,26 +523,69 @@ __device__ __forceinline__ void tma_rows(const FwdArgs& a, const CUtensorMap* tm
     lsu_rows(a, sK, key0, 4 * (__ffs(mm) - 1), 4, r, p, lane, row_bytes, gran);
 }
 
-// Coalesced store of one softmax warp's 32 rows x 64 bytes: lane i holds
-// row i's 64 bytes in v[0..3] (row i = head m0 + i).  The rows go through
-// the warp's 2 KB staging buffer (16-byte slot q of row i at slot
-// q ^ ((i >> 1) & 3): conflict-free both ways) and come back out as eight
-// whole rows per store instruction (lane j: row 8 s + j / 4, slot j % 4).
-// Rows at or past `nlive` (heads >= H) are not written.
-__device__ __forceinline__ void warp_store_rows64(uint8_t* stg, int lane, const uint4 (&v)[4],
+// Coalesced store of one warp's 32 rows x 32 bytes: lane i holds row i's
+// 32 bytes in v[0..1].  The rows go through the warp's 1 KB staging buffer
+// (16-byte slot q of row i at slot q ^ ((i >> 2) & 1): conflict-free both
+// ways) and come back out as 16 rows per store instruction (lane j: row
+// 16 s + j / 2, slot j % 2), i.e. whole 32-byte sectors.  Rows at or past
+// `nlive` (heads >= H) are not written.
+__device__ __forceinline__ void warp_store_rows32(uint8_t* stg, int lane, const uint4 (&v)[2],
                                                   char* seg0, size_t stride, int nlive) {
 #pragma unroll
-  for (int q = 0; q < 4; ++q)
-    *reinterpret_cast<uint4*>(stg + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) = v[q];
+  for (int q = 0; q < 2; ++q)
+    *reinterpret_cast<uint4*>(stg + lane * 32 + ((q ^ ((lane >> 2) & 1)) << 4)) = v[q];
   __syncwarp();
-  const int u = lane & 3;
+  const int u = lane & 1;
 #pragma unroll
-  for (int s = 0; s < 4; ++s) {
-    const int hl = 8 * s + (lane >> 2);
-    const uint4 w = *reinterpret_cast<const uint4*>(stg + hl * 64 + ((u ^ ((hl >> 1) & 3)) << 4));
+  for (int s = 0; s < 2; ++s) {
+    const int hl = 16 * s + (lane >> 1);
+    const uint4 w = *reinterpret_cast<const uint4*>(stg + hl * 32 + ((u ^ ((hl >> 2) & 1)) << 4));
     if (hl < nlive) *reinterpret_cast<uint4*>(seg0 + (size_t)hl * stride + u * 16) = w;
   }
   __syncwarp();
+}
+
+// Epilogue of one 32-column block c of O (this thread's head row): scale by
+// 1 / l and store, as bf16/fp16 into out or as fp32 into the split partials.
+// Column block c is accumulator c / 4, dims (c / 4) * 256 + half * 128 +
+// (c % 4) * 32.  seg_base: the warp's first head row in out or in the
+// partials, as bytes.
+template <bool kBf16>
+__device__ __forceinline__ void epi_block(const uint32_t (&v)[32], int c, int half, float inv,
+                                          bool split, char* seg_base, int dv, uint8_t* stg,
+                                          int lane, int nlive) {
+  const int d0 = (c >> 2) * 256 + half * 128 + (c & 3) * 32;
+  if (split) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 w[2];
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        const int i = 8 * q + 4 * g;
+        w[g] = make_uint4(__float_as_uint(__uint_as_float(v[i]) * inv),
+                          __float_as_uint(__uint_as_float(v[i + 1]) * inv),
+                          __float_as_uint(__uint_as_float(v[i + 2]) * inv),
+                          __float_as_uint(__uint_as_float(v[i + 3]) * inv));
+      }
+      warp_store_rows32(stg, lane, w, seg_base + (size_t)(d0 + 8 * q) * 4, (size_t)dv * 4, nlive);
+    }
+  } else {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint4 w[2];
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        const int i = 16 * h + 8 * g;
+        w[g] = make_uint4(
+            pack2<kBf16>(__uint_as_float(v[i]) * inv, __uint_as_float(v[i + 1]) * inv),
+            pack2<kBf16>(__uint_as_float(v[i + 2]) * inv, __uint_as_float(v[i + 3]) * inv),
+            pack2<kBf16>(__uint_as_float(v[i + 4]) * inv, __uint_as_float(v[i + 5]) * inv),
+            pack2<kBf16>(__uint_as_float(v[i + 6]) * inv, __uint_as_float(v[i + 7]) * inv));
+      }
+      warp_store_rows32(stg, lane, w, seg_base + (size_t)(d0 + 16 * h) * 2, (size_t)dv * 2,
+                        nlive);
+    }
+  }
 }
 
 // S[sb] = Q K^T for the K tile at kb: chunk c accumulates into partial c % 4
@@ -575,7 +662,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int* rows = plan + plan[H_ROWS_OFF];
   constexpr int nchunks = kChunks;  // d_qk / 64
   int* err = args.err;
-  long long* tr = args.trace;
+  long long* tr = ((int)blockIdx.x == args.trace_cta) ? args.trace : nullptr;
 
   // 1024-byte aligned tile area.
   const uint32_t raw = smem_addr(smem_raw);
@@ -599,10 +686,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(smem_addr(&ctl.p_full), kSoftmaxThreads);
     mbar_init(smem_addr(&ctl.pv_done[0]), 1);
     mbar_init(smem_addr(&ctl.pv_done[1]), 1);
-    mbar_init(smem_addr(&ctl.o_free), kSoftmaxThreads);
+    mbar_init(smem_addr(&ctl.o_free), kEpiThreads);
+    mbar_init(smem_addr(&ctl.o_full), 1);
     mbar_init(smem_addr(&ctl.drain), 1);
     mbar_init(smem_addr(&ctl.xbar[0]), kSoftmaxThreads);
     mbar_init(smem_addr(&ctl.xbar[1]), kSoftmaxThreads);
+    mbar_init(smem_addr(&ctl.fin_full[0]), kSoftmaxThreads);
+    mbar_init(smem_addr(&ctl.fin_full[1]), kSoftmaxThreads);
     ctl.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -632,18 +722,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t kv_empty_par = 3u;  // bit = stage
     int stage = 0, produced = 0;
     bool ok = true;
+    RowStream rs(rows, span.r0, span.r1);
     for (int r = span.r0; ok && span.r0 >= 0 && r <= span.r1; ++r) {
-      const Row rv = load_row(rows, r);
+      const Row rv = rs.take(r);
       const int tiles = row_tiles(rv);
       const int ja = (r == span.r0) ? span.t0 : 0;
       const int jb = (r == span.r1) ? span.t1 : (tiles > 0 ? tiles : 1);
       if (tiles == 0 || ja >= jb) continue;
 
-      // ---- key tiles ----
-      const int act_q = args.q_len[rv.b];
-      const int act_kv = args.kv_len[rv.b];
-      const QueryKeys qk = query_keys(args.scenario, act_q, act_kv, rv.s, args.ori_win_left,
-                                      args.cmp_ratio, args.topk);
+      // ---- key tiles (key bounds precomputed by the planner) ----
+      QueryKeys qk;
+      qk.window = rv.window;
+      qk.win_lo = rv.win_lo;
+      qk.cmp = rv.cmp;
+      qk.thr = rv.thr;
+      qk.cmp_len = 0;
       const int W = rv.window;
       const int* idx_row = (args.scenario == SAS_SCENARIO_SCFA)
                                ? args.cmp_indices + (size_t)rv.token * args.topk
@@ -773,8 +866,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0, sbuf = 0, pv_issued = 0, qk_issued = 0, q_seen = 0;
       bool ok = true;
 
+      RowStream rs(rows, span.r0, span.r1);
       for (int r = span.r0; ok && span.r0 >= 0 && r <= span.r1; ++r) {
-        const Row rv = load_row(rows, r);
+        const Row rv = rs.take(r);
         const int tiles = row_tiles(rv);
         const int ja = (r == span.r0) ? span.t0 : 0;
         const int jb = (r == span.r1) ? span.t1 : (tiles > 0 ? tiles : 1);
@@ -845,6 +939,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 trace(tr, 1, 4 * pv_issued + 3);
                 tc_commit(smem_addr(&ctl.kv_empty[st]));
                 tc_commit(smem_addr(&ctl.pv_done[pv_issued & 1]));
+                if (j + 1 == jb) tc_commit(smem_addr(&ctl.o_full));
                 ++pv_issued;
                 need_pv = false;
                 progress = true;
@@ -868,8 +963,68 @@ __global__ void __launch_bounds__(kThreads, 1)
       wait_bar(&ctl, &ctl.drain, 0u, err, 25);
     }
     __syncwarp();
+  } else if (warp >= kEpiWarp0) {
+    // ======================= epilogue =======================
+    // Per (row, piece) with key tiles, in plan order: wait until its O is
+    // complete (o_full, committed after its last PV) and its statistics are
+    // in (fin_full), write O / l and the LSE (or the fp32 split partials),
+    // then release O (o_free) for the next piece's first PV.  Warp w reads
+    // TMEM lanes 32 (w % 4) .. +31: heads (w & 1) * 32 + lane, key half w / 2
+    // of the .ws accumulator layout.
+    const int ew = warp - kEpiWarp0;
+    const int half = ew >> 1;
+    const int m0 = (ew & 1) * 32;
+    const int m = m0 + lane;
+    const int dv = args.head_dim_v;
+    const uint32_t obase = tmem + ((uint32_t)(ew * 32) << 16) + kTmemO;
+    const int nlive = min(32, max(0, args.num_heads - (group * kHeadsPerCta + m0)));
+    uint8_t* stg = ctl.epi[ew];
+    int k = 0;  // pieces finished
+    RowStream rs(rows, span.r0, span.r1);
+    for (int r = span.r0; span.r0 >= 0 && r <= span.r1; ++r) {
+      const Row rv = rs.take(r);
+      const int tiles = row_tiles(rv);
+      const int ja = (r == span.r0) ? span.t0 : 0;
+      const int jb = (r == span.r1) ? span.t1 : (tiles > 0 ? tiles : 1);
+      if (tiles == 0 || ja >= jb) continue;
+      const int fp = k & 1;
+      if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.o_full, (uint32_t)(k & 1), err, 40)))
+        break;
+      if (!__all_sync(0xffffffffu,
+                      wait_bar(&ctl, &ctl.fin_full[fp], (uint32_t)((k >> 1) & 1), err, 41)))
+        break;
+      tc_fence_after();
+      if (ew == 0 && lane == 0) trace(tr, 3, 3 * k + 1);
+      const float m_run = ctl.fin_m[fp][m];
+      const float l_tot = ctl.fin_l[fp][0][m] + ctl.fin_l[fp][1][m];
+      const float inv = (l_tot > 0.f) ? 1.f / l_tot : 0.f;
+      const float lse = (m_run + log2f(l_tot)) * kLn2;
+      const bool split = rv.partial_base >= 0;
+      const int piece = (r == span.r0) ? span.piece0 : 0;
+      const size_t row0 = split ? (size_t)(rv.partial_base + piece) * args.num_heads +
+                                      group * kHeadsPerCta + m0
+                                : (size_t)rv.token * args.num_heads + group * kHeadsPerCta + m0;
+      char* seg_base = split ? reinterpret_cast<char*>(args.o_partial + row0 * dv)
+                             : reinterpret_cast<char*>(args.out) + row0 * dv * 2;
+      for (int c = 0; c < 8; ++c) {
+        uint32_t v[32];
+        tmem_ld32(obase + 32u * c, v);
+        tmem_wait_ld();
+        epi_block<kBf16>(v, c, half, inv, split, seg_base, dv, stg, lane, nlive);
+      }
+      if (half == 0 && lane < nlive) {
+        if (split)
+          args.lse_partial[row0 + lane] = lse;
+        else
+          args.lse[row0 + lane] = lse;
+      }
+      tc_fence_before();
+      mbar_arrive(smem_addr(&ctl.o_free));
+      if (ew == 0 && lane == 0) trace(tr, 3, 3 * k + 2);
+      ++k;
+    }
   } else if (warp < kNumSoftmaxWarps) {
-    // ======================= softmax / epilogue =======================
+    // ======================= softmax =======================
     const int L = threadIdx.x;           // TMEM lane 0..127
     const int m = L & (kHeadsPerCta - 1);  // head row inside the group
     const int half = L >> 6;             // key half / output half
@@ -903,8 +1058,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     const int dv = args.head_dim_v;
 
+    RowStream rs(rows, span.r0, span.r1);
     for (int r = span.r0; ok && span.r0 >= 0 && r <= span.r1; ++r) {
-      const Row rv = load_row(rows, r);
+      const Row rv = rs.take(r);
       const int tiles = row_tiles(rv);
       const int ja = (r == span.r0) ? span.t0 : 0;
       const int jb = (r == span.r1) ? span.t1 : (tiles > 0 ? tiles : 1);
@@ -936,24 +1092,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         uint32_t sraw[32];
         {
+          // S = sum of the four partial accumulators, 16 columns at a time.
           const uint32_t ts = tmem + lane_off + kTmemS + 128u * sb;
-          uint32_t t1[32];
           tmem_ld32(ts, sraw);
-          tmem_ld32(ts + 32u, t1);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            sraw[i] = __float_as_uint(__uint_as_float(sraw[i]) + __uint_as_float(t1[i]));
-          tmem_ld32(ts + 64u, t1);
-          tmem_wait_ld();
+          for (int pp = 1; pp < kQkPartials; ++pp) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            sraw[i] = __float_as_uint(__uint_as_float(sraw[i]) + __uint_as_float(t1[i]));
-          tmem_ld32(ts + 96u, t1);
-          tmem_wait_ld();
+            for (int h16 = 0; h16 < 2; ++h16) {
+              uint32_t t1[16];
+              tmem_ld16(ts + 32u * pp + 16u * h16, t1);
+              tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            sraw[i] = __float_as_uint(__uint_as_float(sraw[i]) + __uint_as_float(t1[i]));
+              for (int i = 0; i < 16; ++i)
+                sraw[16 * h16 + i] =
+                    __float_as_uint(__uint_as_float(sraw[16 * h16 + i]) + __uint_as_float(t1[i]));
+            }
+          }
         }
         tc_fence_before();
         mbar_arrive(smem_addr(&ctl.s_empty[sb]));
@@ -1024,76 +1179,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++pv_count;
       }
       if (!ok) break;
-      // ---- epilogue of this (row, piece) ----
+      // ---- hand this (row, piece)'s statistics to the epilogue (producer
+      // warps); m_run is identical in both key halves ----
+      const int fp = rows_done & 1;
+      if (half == 0) ctl.fin_m[fp][m] = m_run;
+      ctl.fin_l[fp][half][m] = l_run;
+      mbar_arrive(smem_addr(&ctl.fin_full[fp]));
       if (threadIdx.x == 0) trace(tr, 3, 3 * rows_done);
-      if (!__all_sync(0xffffffffu, wait_pv(pv_count - 1, 33))) {
-        ok = false;
-        break;
-      }
-      if (threadIdx.x == 0) trace(tr, 3, 3 * rows_done + 1);
-      tc_fence_after();
-      ctl.red[xpar][half][m] = l_run;
-      if (!__all_sync(0xffffffffu, exchange(35))) { ok = false; break; }
-      const float l_tot = l_run + ctl.red[xpar][half ^ 1][m];
-      xpar ^= 1;
-      const bool split = rv.partial_base >= 0;
-      const float inv = (l_tot > 0.f) ? 1.f / l_tot : 0.f;
-      const float lse = (m_run + log2f(l_tot)) * kLn2;
-      // Heads of this warp: group * 64 + m0 + i, i = lane (m0 = 0 or 32).
-      const int m0 = (warp & 1) * 32;
-      const int nlive = min(32, max(0, args.num_heads - (group * kHeadsPerCta + m0)));
-      const size_t row0 = (size_t)rv.token * args.num_heads + group * kHeadsPerCta + m0;
-      const int piece = (r == span.r0) ? span.piece0 : 0;
-      const size_t prow0 =
-          split ? (size_t)(rv.partial_base + piece) * args.num_heads + group * kHeadsPerCta + m0
-                : 0;
-      uint8_t* stg = ctl.epi[warp];
-      for (int c = 0; c < 8; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tmem + lane_off + kTmemO + 32u * c, v);
-        tmem_wait_ld();
-        // Column block c: accumulator hv = c / 4, dims hv*256 + half*128 + (c%4)*32.
-        const int d0 = (c >> 2) * 256 + half * 128 + (c & 3) * 32;
-        if (split) {
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            uint4 w[4];
-#pragma unroll
-            for (int g = 0; g < 4; ++g) {
-              const int i = 16 * hh + 4 * g;
-              w[g] = make_uint4(__float_as_uint(__uint_as_float(v[i]) * inv),
-                                __float_as_uint(__uint_as_float(v[i + 1]) * inv),
-                                __float_as_uint(__uint_as_float(v[i + 2]) * inv),
-                                __float_as_uint(__uint_as_float(v[i + 3]) * inv));
-            }
-            char* seg0 = reinterpret_cast<char*>(args.o_partial + prow0 * dv + d0 + 16 * hh);
-            warp_store_rows64(stg, lane, w, seg0, (size_t)dv * 4, nlive);
-          }
-        } else {
-          uint4 w[4];
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const int i = 8 * g;
-            w[g] = make_uint4(
-                pack2<kBf16>(__uint_as_float(v[i]) * inv, __uint_as_float(v[i + 1]) * inv),
-                pack2<kBf16>(__uint_as_float(v[i + 2]) * inv, __uint_as_float(v[i + 3]) * inv),
-                pack2<kBf16>(__uint_as_float(v[i + 4]) * inv, __uint_as_float(v[i + 5]) * inv),
-                pack2<kBf16>(__uint_as_float(v[i + 6]) * inv, __uint_as_float(v[i + 7]) * inv));
-          }
-          char* seg0 = reinterpret_cast<char*>(args.out) + (row0 * dv + d0) * 2;
-          warp_store_rows64(stg, lane, w, seg0, (size_t)dv * 2, nlive);
-        }
-      }
-      if (live && half == 0) {
-        if (split) {
-          args.lse_partial[(size_t)(rv.partial_base + piece) * args.num_heads + head] = lse;
-        } else {
-          args.lse[orow] = lse;
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(smem_addr(&ctl.o_free));
-      if (threadIdx.x == 0) trace(tr, 3, 3 * rows_done + 2);
       ++rows_done;
     }
   }

@@ -15,13 +15,14 @@ constexpr int kMaxHeadGroups = 2;  // H <= 128
 
 // Serialised plan (int32), all sections 64-element aligned:
 //   header[kHeaderInts]
-//   rows[num_rows][kRowInts]      one per query token (incl. padded BSND rows)
+//   rows[num_rows][kRowInts]      one per query token (incl. padded BSND rows),
+//                                 with its key bounds (query_keys) precomputed
 //   workers[num_workers][kWorkerInts]  begin_row, begin_tile, end_row, end_tile,
 //                                 piece ordinal of begin_row (0 if begin_tile = 0)
 //   split[num_split_rows][4]      token, pieces, partial_base, pad
 //   batch: act_q[B] then (64-aligned) act_kv[B]
 constexpr int kHeaderInts = 16;
-constexpr int kRowInts = 8;
+constexpr int kRowInts = 12;
 constexpr int kWorkerInts = 8;
 enum HeaderField {
   H_MAGIC = 0, H_NUM_ROWS, H_NUM_WORKERS, H_HEAD_GROUPS, H_NUM_SPLIT, H_NUM_PARTIALS,
@@ -35,7 +36,11 @@ enum RowField {
   R_FLAGS,         // bit0: padded BSND slot (write zeros)
   R_FIRST_WORKER,  // first worker that processes a tile of this row (diagnostic)
   R_PARTIAL_BASE,  // partial slot of piece 0, or -1 when the row is not split
-  R_WINDOW         // window slots W (slots [0, W) are window keys)
+  R_WINDOW,        // window slots W (slots [0, W) are window keys)
+  R_WIN_LO,        // first logical window position
+  R_CMP,           // compressed slots scanned
+  R_THR,           // causal threshold of the compressed positions
+  R_PAD            // unused
 };
 constexpr int kRowPadded = 1;
 constexpr int32_t kPlanMagic = 0x53415331;  // "SAS1"

@@ -21,7 +21,8 @@ struct FwdArgs {
   void* out;
   float* lse;
   int32_t* err;
-  long long* trace;         // optional clock trace of CTA 0 (diagnostics)
+  long long* trace;         // optional clock trace of one CTA (diagnostics)
+  int32_t trace_cta;        // CTA traced (SAS_TRACE_CTA, default 0)
   const int32_t* plan;      // device copy of the serialised plan
   const int32_t* q_len;     // [B] device (act_q per batch)
   const int32_t* kv_len;    // [B] device (seqused_kv)

@@ -28,7 +28,7 @@ constexpr int64_t kRowCost = 1;   // Q load + epilogue, in tile units
 constexpr int64_t kTileCost = 1;
 
 struct Row {
-  int32_t token, b, s, slots, flags, window;
+  int32_t token, b, s, slots, flags, window, win_lo, cmp, thr;
 };
 
 int collect_rows(const SasProblem& p, std::vector<Row>* rows) {
@@ -52,7 +52,7 @@ int collect_rows(const SasProblem& p, std::vector<Row>* rows) {
     }
     if ((int64_t)start + span > p.total_tokens) return SAS_ERR_INVALID;
     for (int32_t s = 0; s < span; ++s) {
-      Row r{start + s, b, s, 0, 0, 0};
+      Row r{start + s, b, s, 0, 0, 0, 0, 0, 0};
       if (s >= len) {
         r.flags = sas::kRowPadded;
       } else {
@@ -60,6 +60,9 @@ int collect_rows(const SasProblem& p, std::vector<Row>* rows) {
                                            p.topk);
         r.window = k.window;
         r.slots = k.window + k.cmp;
+        r.win_lo = k.win_lo;
+        r.cmp = k.cmp;
+        r.thr = k.thr;
       }
       rows->push_back(r);
     }
@@ -183,6 +186,10 @@ int build(const SasProblem& p, int32_t num_sms, bool fill, Built* out) {
     e[sas::R_FIRST_WORKER] = first_w[r];
     e[sas::R_PARTIAL_BASE] = partial_base[r];
     e[sas::R_WINDOW] = rows[r].window;
+    e[sas::R_WIN_LO] = rows[r].win_lo;
+    e[sas::R_CMP] = rows[r].cmp;
+    e[sas::R_THR] = rows[r].thr;
+    e[sas::R_PAD] = 0;
   }
   for (int64_t w = 0; w < nw; ++w) {
     int32_t* e = &pl[workers_off + w * sas::kWorkerInts];

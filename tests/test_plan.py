@@ -46,10 +46,13 @@ def build_plan(p, sms):
     return np.frombuffer(buf, dtype=np.int32).copy(), info
 
 
+ROW_INTS = 12  # token, b, s, slots, flags, first_worker, partial_base, window, win_lo, cmp, thr, pad
+
+
 def rows_of(plan):
     n = plan[HDR["rows"]]
     off = plan[HDR["rows_off"]]
-    return plan[off: off + 8 * n].reshape(n, 8)
+    return plan[off: off + ROW_INTS * n].reshape(n, ROW_INTS)
 
 
 def segments(plan):
@@ -128,7 +131,7 @@ def kernel_slot_positions(case, plan):
         idx = idx.reshape(-1, idx.shape[-1]).numpy()
     K = idx.shape[1] if idx is not None else 0
     for w, r, ja, jb, piece in segments(plan):
-        t, b, s, slots, flags, _, _, Wn = rows[r]
+        t, b, s, slots, flags, _, _, Wn, row_lo, row_cmp, row_thr, _ = rows[r]
         if flags & 1 or slots == 0:
             continue
         aq = int(case.meta["q_len"][b])
@@ -138,6 +141,8 @@ def kernel_slot_positions(case, plan):
         lo = max(s_g - case.ori_win_left, 0)
         thr = (akv - aq + s + 1) // case.cmp_ratio if scen >= 2 else 0
         ncmp = min(max(thr, 0), K) if scen == 3 else max(thr, 0)
+        # the key bounds the planner precomputes for the kernel
+        assert (row_lo, row_cmp, row_thr) == (lo, ncmp, thr), (r, row_lo, row_cmp, row_thr)
         stopped = False
         if scen == 3 and ja > 0:
             lim = min(ja * 64 - Wn, ncmp)
