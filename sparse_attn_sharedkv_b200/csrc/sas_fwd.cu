@@ -69,6 +69,10 @@ constexpr int kSoftmaxThreads = 32 * kNumSoftmaxWarps;
 constexpr int kProducerThreads = 32 * kNumProducerWarps;
 
 constexpr int kQkPartials = 4;     // independent S accumulators per tile (QK chains)
+// A K stage completes in three chunk groups (chunks 3g .. 3g + 2), each with
+// its own barrier, so QK starts on the first chunks while the rest land.
+constexpr int kChunkGroups = 3;
+__host__ __device__ constexpr int chunk_group(int c) { return c / 3; }
 
 constexpr int kMaxChunks = 9;                   // d_qk / 64
 constexpr int kChunkBytes = kHeadsPerCta * 128;  // 64 rows x 64 bf16 = 8 KB
@@ -296,7 +300,7 @@ __device__ __forceinline__ uint32_t swz(int row, int granule) {
 }
 
 struct Ctl {
-  uint64_t kv_full[2];
+  uint64_t kv_full[2][kChunkGroups];  // [stage][chunk group]
   uint64_t kv_empty[2];
   uint64_t q_full, q_empty;
   uint64_t s_full[2];
@@ -485,11 +489,12 @@ __device__ __forceinline__ void lsu_rows(const FwdArgs& a, uint32_t sK, int key0
 // 64-column chunk (4 rows x 128 B into 512 B of the swizzled chunk).  Slots
 // without a source read an out-of-range row, which TMA fills with zeros.  A
 // group whose rows come from both caches (window / compressed boundary) is
-// moved by cp.async instead.  Lane 0 arms the barrier with the TMA bytes.
+// moved by cp.async instead.  Lane 0 arms the chunk-group barriers with the
+// TMA bytes each of them receives.
 __device__ __forceinline__ void tma_rows(const FwdArgs& a, const CUtensorMap* tm_ori,
                                          const CUtensorMap* tm_cmp, int nchunks, uint32_t sK,
-                                         uint32_t bar, int key0, int r, int p, int lane,
-                                         uint32_t row_bytes, int gran) {
+                                         const uint32_t (&bar)[kChunkGroups], int key0, int r,
+                                         int p, int lane, uint32_t row_bytes, int gran) {
   const int g = lane & 3;
   int row[4], pool[4];
 #pragma unroll
@@ -507,7 +512,12 @@ __device__ __forceinline__ void tma_rows(const FwdArgs& a, const CUtensorMap* tm
     }
   }
   const uint32_t mixed_mask = __ballot_sync(0xffffffffu, mixed) & 0xFu;
-  if (lane == 0) mbar_expect_tx(bar, (uint32_t)(4 - __popc(mixed_mask)) * 4u * row_bytes);
+  if (lane == 0) {
+    const uint32_t groups = (uint32_t)(4 - __popc(mixed_mask));
+#pragma unroll
+    for (int cg = 0; cg < kChunkGroups; ++cg)
+      mbar_expect_tx(bar[cg], groups * 4u * 128u * (uint32_t)min(3, nchunks - 3 * cg));
+  }
   __syncwarp();
   if (lane < 4 && !mixed) {
     const CUtensorMap* m = (P == 1) ? tm_cmp : tm_ori;
@@ -517,7 +527,8 @@ __device__ __forceinline__ void tma_rows(const FwdArgs& a, const CUtensorMap* tm
       if (pool[i] < 0 || row[i] < 0) row[i] = sentinel;
     const uint32_t dst = sK + (uint32_t)(key0 + 4 * lane) * 128u;
     for (int c = 0; c < nchunks; ++c)
-      tma_gather4(dst + c * kChunkBytes, m, c * 64, row[0], row[1], row[2], row[3], bar);
+      tma_gather4(dst + c * kChunkBytes, m, c * 64, row[0], row[1], row[2], row[3],
+                  bar[chunk_group(c)]);
   }
   for (uint32_t mm = mixed_mask; mm != 0u; mm &= mm - 1u)
     lsu_rows(a, sK, key0, 4 * (__ffs(mm) - 1), 4, r, p, lane, row_bytes, gran);
@@ -588,36 +599,27 @@ __device__ __forceinline__ void epi_block(const uint32_t (&v)[32], int c, int ha
   }
 }
 
-// S[sb] = Q K^T for the K tile at kb: chunk c accumulates into partial c % 4
-// and consecutive MMAs rotate over the partials, so four dependent chains
-// overlap in the pipe.  Descriptors are built once and advanced by constant
-// offsets (all shared addresses are below 256 KB, so the 14-bit address
-// field never carries).  Fully unrolled: the issuing thread spends a few
-// instructions per MMA.
+// Chunk group cg of S[sb] = Q K^T for the K tile at kb (chunks 3 cg ..
+// 3 cg + 2): chunk c accumulates into partial c % 4, so consecutive MMAs
+// rotate over the partials and four dependent chains overlap in the pipe;
+// a partial's first chunk (c < 4) starts it at ks = 0.  Descriptors are
+// built once and advanced by constant offsets (all shared addresses are
+// below 256 KB, so the 14-bit address field never carries).
 template <int kChunks>
-__device__ __forceinline__ void issue_qk(uint32_t d, uint32_t sQ, uint32_t kb, uint32_t idesc) {
+__device__ __forceinline__ void issue_qk_group(uint32_t d, uint32_t sQ, uint32_t kb,
+                                               uint32_t idesc, int cg) {
   const uint64_t dq = smem_desc(sQ, 16, 1024);
   const uint64_t dk = smem_desc(kb, 16, 1024);
-#pragma unroll 1
-  for (int c4 = 0; c4 < kChunks; c4 += kQkPartials) {
-    const uint64_t c4off = (uint64_t)((c4 * kChunkBytes) >> 4);
-    const uint32_t acc0 = c4 == 0 ? 0u : 1u;
-    if (c4 + kQkPartials <= kChunks) {
+  const int c0 = 3 * cg;
+  const int nc = min(3, kChunks - c0);
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
+  for (int ks = 0; ks < 4; ++ks) {
 #pragma unroll
-        for (int pp = 0; pp < kQkPartials; ++pp) {
-          const uint64_t off = c4off + (uint64_t)((pp * kChunkBytes + ks * 32) >> 4);
-          mma_ws(d + 32u * pp, dq + off, dk + off, idesc, ks == 0 ? acc0 : 1u);
-        }
-      }
-    } else {
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        for (int pp = 0; pp < kChunks - c4; ++pp) {
-          const uint64_t off = c4off + (uint64_t)((pp * kChunkBytes + ks * 32) >> 4);
-          mma_ws(d + 32u * pp, dq + off, dk + off, idesc, ks == 0 ? acc0 : 1u);
-        }
+    for (int i = 0; i < 3; ++i) {
+      if (i < nc) {
+        const int c = c0 + i;
+        const uint64_t off = (uint64_t)((c * kChunkBytes + ks * 32) >> 4);
+        mma_ws(d + 32u * (c & 3), dq + off, dk + off, idesc, (c < 4 && ks == 0) ? 0u : 1u);
       }
     }
   }
@@ -637,6 +639,48 @@ __device__ __forceinline__ void issue_pv(uint32_t o, uint32_t kb, uint32_t idesc
              (first && ks == 0) ? 0u : 1u);
     }
   }
+}
+
+// Slots of tile j resolved by producer warp pw: keys 16 pw .. 16 pw + 15
+// (lanes 16..31 mirror lanes 0..15).  `stopped`: a -1 occurred in an
+// earlier tile of the row (the compressed scan stops there); each warp
+// scans the whole tile for -1, so the stop prefix needs no cross-warp
+// exchange.  Returns the slot source, its valid ballot in *valid.
+__device__ __forceinline__ SlotSrc resolve_tile(const FwdArgs& a, const Row& rv,
+                                                const QueryKeys& qk, const int* idx_row, int j,
+                                                int pw, int lane, bool* stopped,
+                                                uint32_t* valid, int* err) {
+  uint64_t m1mask = 0;
+  if (idx_row != nullptr) {
+    const int ca = j * kTileKeys + lane - rv.window;
+    const int cb = ca + 32;
+    const bool ma = (ca >= 0 && ca < qk.cmp) && (__ldg(idx_row + ca) == -1);
+    const bool mb = (cb >= 0 && cb < qk.cmp) && (__ldg(idx_row + cb) == -1);
+    m1mask = (uint64_t)__ballot_sync(0xffffffffu, ma) |
+             ((uint64_t)__ballot_sync(0xffffffffu, mb) << 32);
+  }
+  const int ka = pw * 16 + (lane & 15);
+  const bool blk = *stopped || ((m1mask & ((1ull << ka) - 1ull)) != 0);
+  const SlotSrc src = resolve_slot(a, rv, qk, j * kTileKeys + ka, idx_row, blk, err);
+  if (m1mask != 0) *stopped = true;
+  *valid = __ballot_sync(0xffffffffu, src.valid);
+  return src;
+}
+
+// L2 prefetch of this warp's 16 compressed-cache key rows of a later tile (lane l: row
+// l % 16, lines [0, 5) or [5, row_bytes / 128) of it), so that the tile's
+// TMA gathers, issued once its stage is free, read L2 instead of HBM.
+__device__ __forceinline__ void prefetch_rows(const FwdArgs& a, const SlotSrc& src, int lane,
+                                              uint32_t row_bytes) {
+  // Window rows (cache 0) are recent and contiguous, typically L2-resident.
+  if (src.pool != 1 || src.row < 0) return;
+  const char* base = reinterpret_cast<const char*>(src.pool == 1 ? a.cmp_kv : a.ori_kv) +
+                     (size_t)src.row * row_bytes;
+  const int lines = (int)(row_bytes >> 7);
+  const int l0 = lane < 16 ? 0 : 5;
+  const int l1 = lane < 16 ? 5 : lines;
+  for (int l = l0; l < l1; ++l)
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(base + l * 128) : "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -676,7 +720,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Per producer warp: one arrival from lane 0 after the valid bits are
       // written (arming the TMA bytes in TMA mode) and one cp.async
       // completion arrival per lane.
-      mbar_init(smem_addr(&ctl.kv_full[i]), kNumProducerWarps + kProducerThreads);
+      for (int g = 0; g < kChunkGroups; ++g)
+        mbar_init(smem_addr(&ctl.kv_full[i][g]), kNumProducerWarps + kProducerThreads);
       mbar_init(smem_addr(&ctl.kv_empty[i]), 1);
       mbar_init(smem_addr(&ctl.s_full[i]), 1);
       mbar_init(smem_addr(&ctl.s_empty[i]), kSoftmaxThreads);
@@ -737,39 +782,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       qk.cmp = rv.cmp;
       qk.thr = rv.thr;
       qk.cmp_len = 0;
-      const int W = rv.window;
       const int* idx_row = (args.scenario == SAS_SCENARIO_SCFA)
                                ? args.cmp_indices + (size_t)rv.token * args.topk
                                : nullptr;
       // Slots before this piece may hold a -1 that stops the scan.
       bool stopped = false;
       if (idx_row != nullptr && ja > 0) {
-        const int lim = min(ja * kTileKeys - W, qk.cmp);
+        const int lim = min(ja * kTileKeys - rv.window, qk.cmp);
         for (int c0 = 0; c0 < lim && !stopped; c0 += 32) {
           const int c = c0 + lane;
           const bool m1 = (c < lim) && (__ldg(idx_row + c) == -1);
           stopped = __any_sync(0xffffffffu, m1);
         }
       }
+      // Tiles are resolved one ahead; head group 0 prefetches the next
+      // tile's rows into L2 (the other group reads the same rows).
+      uint32_t va = 0;
+      SlotSrc nxt = resolve_tile(args, rv, qk, idx_row, ja, pw, lane, &stopped, &va, err);
       for (int j = ja; j < jb; ++j) {
-        // -1 positions among the tile's compressed slots (each warp scans the
-        // whole tile, so the stop prefix needs no cross-warp exchange).
-        uint64_t m1mask = 0;
-        if (idx_row != nullptr) {
-          const int ca = j * kTileKeys + lane - W;
-          const int cb = ca + 32;
-          const bool ma = (ca >= 0 && ca < qk.cmp) && (__ldg(idx_row + ca) == -1);
-          const bool mb = (cb >= 0 && cb < qk.cmp) && (__ldg(idx_row + cb) == -1);
-          m1mask = (uint64_t)__ballot_sync(0xffffffffu, ma) |
-                   ((uint64_t)__ballot_sync(0xffffffffu, mb) << 32);
+        const SlotSrc sa = nxt;
+        const uint32_t va_cur = va;
+        if (j + 1 < jb) {
+          nxt = resolve_tile(args, rv, qk, idx_row, j + 1, pw, lane, &stopped, &va, err);
+          if (group == 0) prefetch_rows(args, nxt, lane, row_bytes);
         }
-        // Slots resolved by this warp: keys 16 pw .. 16 pw + 15 (lanes 16..31
-        // mirror lanes 0..15).
-        const int ka = pw * 16 + (lane & 15);
-        const bool blk_a = stopped || ((m1mask & ((1ull << ka) - 1ull)) != 0);
-        const SlotSrc sa = resolve_slot(args, rv, qk, j * kTileKeys + ka, idx_row, blk_a, err);
-        if (m1mask != 0) stopped = true;
-        const uint32_t va = __ballot_sync(0xffffffffu, sa.valid);
         if (leader && lane == 0) trace(tr, 0, 3 * produced);
         if (!__all_sync(0xffffffffu,
                         wait_bar(&ctl, &ctl.kv_empty[stage], (kv_empty_par >> stage) & 1u, err, 2))) {
@@ -778,12 +814,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (leader && lane == 0) trace(tr, 0, 3 * produced + 1);
         kv_empty_par ^= 1u << stage;
-        const uint32_t bar = smem_addr(&ctl.kv_full[stage]);
+        uint32_t bar[kChunkGroups];
+#pragma unroll
+        for (int cg = 0; cg < kChunkGroups; ++cg) bar[cg] = smem_addr(&ctl.kv_full[stage][cg]);
         const uint32_t sK = sK0 + stage * kStageBytes;
-        if (lane == 0) ctl.valid[stage][pw] = (uint16_t)(va & 0xffffu);
+        if (lane == 0) ctl.valid[stage][pw] = (uint16_t)(va_cur & 0xffffu);
         if (lsu) {
           __syncwarp();
-          if (lane == 0) mbar_arrive(bar);
+          if (lane == 0) {
+#pragma unroll
+            for (int cg = 0; cg < kChunkGroups; ++cg) mbar_arrive(bar[cg]);
+          }
           lsu_rows(args, sK, pw * 16, 0, 16, sa.row, sa.pool, lane, row_bytes, gran);
         } else {
           // The warp's 16 slots read 16 consecutive rows of one cache (window
@@ -796,19 +837,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                          sa.row == row0 + (lane & 15));
           if (run16) {
             if (lane == 0) {
-              mbar_expect_tx(bar, 16u * row_bytes);
+#pragma unroll
+              for (int cg = 0; cg < kChunkGroups; ++cg)
+                mbar_expect_tx(bar[cg], 16u * 128u * (uint32_t)min(3, nchunks - 3 * cg));
               const CUtensorMap* m = (pool0 == 1) ? &tm_cmp16 : &tm_ori16;
               const uint32_t dst = sK + (uint32_t)(pw * 16) * 128u;
 #pragma unroll
               for (int c = 0; c < nchunks; ++c)
-                tma_load_2d(dst + c * kChunkBytes, m, c * 64, row0, bar);
+                tma_load_2d(dst + c * kChunkBytes, m, c * 64, row0, bar[chunk_group(c)]);
             }
           } else {
             tma_rows(args, &tm_ori, &tm_cmp, nchunks, sK, bar, pw * 16, sa.row, sa.pool, lane,
                      row_bytes, gran);
           }
         }
-        cp_async_arrive_noinc(bar);
+#pragma unroll
+        for (int cg = 0; cg < kChunkGroups; ++cg) cp_async_arrive_noinc(bar[cg]);
         if (leader && lane == 0) trace(tr, 0, 3 * produced + 2);
         ++produced;
         stage ^= 1;
@@ -876,14 +920,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!wait_bar(&ctl, &ctl.q_full, q_full_par, err, 22)) { ok = false; break; }
         q_full_par ^= 1u;
         trace(tr, 3, 6144 + q_seen++);
-        if (!wait_bar(&ctl, &ctl.kv_full[stage], (kv_full_par >> stage) & 1u, err, 20)) { ok = false; break; }
-        kv_full_par ^= 1u << stage;
         if (!wait_bar(&ctl, &ctl.s_empty[sbuf], (s_empty_par >> sbuf) & 1u, err, 21)) { ok = false; break; }
         s_empty_par ^= 1u << sbuf;
-        fence_proxy_async();
-        tc_fence_after();
         trace(tr, 1, 4 * qk_issued);
-        issue_qk<nchunks>(tmem + kTmemS + 128u * sbuf, sQ, sK0 + stage * kStageBytes, idesc_qk);
+        for (int cg = 0; cg < kChunkGroups && ok; ++cg) {
+          if (!wait_bar(&ctl, &ctl.kv_full[stage][cg], (kv_full_par >> stage) & 1u, err, 20)) {
+            ok = false;
+            break;
+          }
+          fence_proxy_async();
+          tc_fence_after();
+          issue_qk_group<nchunks>(tmem + kTmemS + 128u * sbuf, sQ, sK0 + stage * kStageBytes,
+                                  idesc_qk, cg);
+        }
+        if (!ok) break;
+        kv_full_par ^= 1u << stage;
         trace(tr, 1, 4 * qk_issued + 1);
         ++qk_issued;
         tc_commit(smem_addr(&ctl.s_full[sbuf]));
@@ -894,34 +945,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           sbuf ^= 1;
           // Issue QK(j+1) and PV(j) in whichever order their inputs arrive
           // (QK first when both are ready, so softmax(j+1) overlaps PV(j)).
-          bool need_qk = (j + 1 < jb), kv_ok = false, s_ok = false;
+          bool need_qk = (j + 1 < jb), s_ok = false;
+          int qg = 0;  // chunk groups of QK(j+1) issued
           bool need_pv = true, p_ok = false, o_ok = (j != ja);
           long long t0 = clock64();
+          // PV(j) first as soon as P(j) is ready: it releases the K stage that
+          // the gather of tile j + 2 waits for.  QK(j+1) goes one chunk group
+          // at a time, as the groups land.
           while (need_qk || need_pv) {
             bool progress = false;
-            if (need_qk) {
-              if (!kv_ok && mbar_test(smem_addr(&ctl.kv_full[stage]), (kv_full_par >> stage) & 1u)) {
-                kv_ok = true;
-                kv_full_par ^= 1u << stage;
-              }
-              if (!s_ok && mbar_test(smem_addr(&ctl.s_empty[sbuf]), (s_empty_par >> sbuf) & 1u)) {
-                s_ok = true;
-                s_empty_par ^= 1u << sbuf;
-              }
-              if (kv_ok && s_ok) {
-                fence_proxy_async();
-                tc_fence_after();
-                trace(tr, 1, 4 * qk_issued);
-                issue_qk<nchunks>(tmem + kTmemS + 128u * sbuf, sQ, sK0 + stage * kStageBytes,
-                                  idesc_qk);
-                trace(tr, 1, 4 * qk_issued + 1);
-                ++qk_issued;
-                tc_commit(smem_addr(&ctl.s_full[sbuf]));
-                if (j + 2 == jb) tc_commit(smem_addr(&ctl.q_empty));
-                need_qk = false;
-                progress = true;
-              }
-            }
             if (need_pv) {
               if (!p_ok && mbar_test(smem_addr(&ctl.p_full), p_full_par)) {
                 p_ok = true;
@@ -943,6 +975,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ++pv_issued;
                 need_pv = false;
                 progress = true;
+              }
+            }
+            if (need_qk) {
+              if (!s_ok && mbar_test(smem_addr(&ctl.s_empty[sbuf]), (s_empty_par >> sbuf) & 1u)) {
+                s_ok = true;
+                s_empty_par ^= 1u << sbuf;
+                trace(tr, 1, 4 * qk_issued);
+              }
+              if (s_ok && qg < kChunkGroups &&
+                  mbar_test(smem_addr(&ctl.kv_full[stage][qg]), (kv_full_par >> stage) & 1u)) {
+                fence_proxy_async();
+                tc_fence_after();
+                issue_qk_group<nchunks>(tmem + kTmemS + 128u * sbuf, sQ,
+                                        sK0 + stage * kStageBytes, idesc_qk, qg);
+                ++qg;
+                progress = true;
+              }
+              if (qg == kChunkGroups) {
+                kv_full_par ^= 1u << stage;
+                trace(tr, 1, 4 * qk_issued + 1);
+                ++qk_issued;
+                tc_commit(smem_addr(&ctl.s_full[sbuf]));
+                if (j + 2 == jb) tc_commit(smem_addr(&ctl.q_empty));
+                need_qk = false;
               }
             }
             if (!progress) {
@@ -1086,7 +1142,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.s_full[sb], (s_full_par >> sb) & 1u, err, 30))) { ok = false; break; }
         s_full_par ^= 1u << sb;
         if (threadIdx.x == 0) trace(tr, 2, 4 * pv_count + 3);
-        if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.kv_full[st], (kv_full_par >> st) & 1u, err, 31))) { ok = false; break; }
+        if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.kv_full[st][0], (kv_full_par >> st) & 1u, err, 31))) { ok = false; break; }
         kv_full_par ^= 1u << st;
         if (threadIdx.x == 0) trace(tr, 2, 4 * pv_count);
         tc_fence_after();
