@@ -908,6 +908,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t kv_full_par = 0u, s_empty_par = 3u;
       uint32_t q_full_par = 0u, p_full_par = 0u, o_free_par = 1u;
       int stage = 0, sbuf = 0, pv_issued = 0, qk_issued = 0, q_seen = 0;
+      const bool pv_first = args.scenario == SAS_SCENARIO_SCFA;
       bool ok = true;
 
       RowStream rs(rows, span.r0, span.r1);
@@ -949,56 +950,63 @@ __global__ void __launch_bounds__(kThreads, 1)
           int qg = 0;  // chunk groups of QK(j+1) issued
           bool need_pv = true, p_ok = false, o_ok = (j != ja);
           long long t0 = clock64();
-          // PV(j) first as soon as P(j) is ready: it releases the K stage that
-          // the gather of tile j + 2 waits for.  QK(j+1) goes one chunk group
-          // at a time, as the groups land.
+          // QK(j+1) goes one chunk group at a time, as the groups land.  Top-k
+          // tiles (gathered row by row) issue PV(j) first, since it releases
+          // the stage the gather of tile j + 2 waits for; window / compressed
+          // runs (fast box loads) issue landed QK groups first, so softmax(j+1)
+          // overlaps PV(j).
           while (need_qk || need_pv) {
             bool progress = false;
-            if (need_pv) {
-              if (!p_ok && mbar_test(smem_addr(&ctl.p_full), p_full_par)) {
-                p_ok = true;
-                p_full_par ^= 1u;
-              }
-              if (!o_ok && mbar_test(smem_addr(&ctl.o_free), o_free_par)) {
-                o_ok = true;
-                o_free_par ^= 1u;
-              }
-              if (p_ok && o_ok) {
-                trace(tr, 1, 4 * pv_issued + 2);
-                fence_proxy_async();
-                tc_fence_after();
-                issue_pv(tmem + kTmemO, sK0 + st * kStageBytes, idesc_pv, j == ja);
-                trace(tr, 1, 4 * pv_issued + 3);
-                tc_commit(smem_addr(&ctl.kv_empty[st]));
-                tc_commit(smem_addr(&ctl.pv_done[pv_issued & 1]));
-                if (j + 1 == jb) tc_commit(smem_addr(&ctl.o_full));
-                ++pv_issued;
-                need_pv = false;
-                progress = true;
-              }
-            }
-            if (need_qk) {
-              if (!s_ok && mbar_test(smem_addr(&ctl.s_empty[sbuf]), (s_empty_par >> sbuf) & 1u)) {
-                s_ok = true;
-                s_empty_par ^= 1u << sbuf;
-                trace(tr, 1, 4 * qk_issued);
-              }
-              if (s_ok && qg < kChunkGroups &&
-                  mbar_test(smem_addr(&ctl.kv_full[stage][qg]), (kv_full_par >> stage) & 1u)) {
-                fence_proxy_async();
-                tc_fence_after();
-                issue_qk_group<nchunks>(tmem + kTmemS + 128u * sbuf, sQ,
-                                        sK0 + stage * kStageBytes, idesc_qk, qg);
-                ++qg;
-                progress = true;
-              }
-              if (qg == kChunkGroups) {
-                kv_full_par ^= 1u << stage;
-                trace(tr, 1, 4 * qk_issued + 1);
-                ++qk_issued;
-                tc_commit(smem_addr(&ctl.s_full[sbuf]));
-                if (j + 2 == jb) tc_commit(smem_addr(&ctl.q_empty));
-                need_qk = false;
+            for (int pass = 0; pass < 2; ++pass) {
+              if ((pass == 0) != pv_first) {
+                if (need_qk) {
+                  if (!s_ok && mbar_test(smem_addr(&ctl.s_empty[sbuf]), (s_empty_par >> sbuf) & 1u)) {
+                    s_ok = true;
+                    s_empty_par ^= 1u << sbuf;
+                    trace(tr, 1, 4 * qk_issued);
+                  }
+                  if (s_ok && qg < kChunkGroups &&
+                      mbar_test(smem_addr(&ctl.kv_full[stage][qg]), (kv_full_par >> stage) & 1u)) {
+                    fence_proxy_async();
+                    tc_fence_after();
+                    issue_qk_group<nchunks>(tmem + kTmemS + 128u * sbuf, sQ,
+                                            sK0 + stage * kStageBytes, idesc_qk, qg);
+                    ++qg;
+                    progress = true;
+                  }
+                  if (qg == kChunkGroups) {
+                    kv_full_par ^= 1u << stage;
+                    trace(tr, 1, 4 * qk_issued + 1);
+                    ++qk_issued;
+                    tc_commit(smem_addr(&ctl.s_full[sbuf]));
+                    if (j + 2 == jb) tc_commit(smem_addr(&ctl.q_empty));
+                    need_qk = false;
+                  }
+                }
+              } else {
+                if (need_pv && (pv_first || !progress)) {
+                  if (!p_ok && mbar_test(smem_addr(&ctl.p_full), p_full_par)) {
+                    p_ok = true;
+                    p_full_par ^= 1u;
+                  }
+                  if (!o_ok && mbar_test(smem_addr(&ctl.o_free), o_free_par)) {
+                    o_ok = true;
+                    o_free_par ^= 1u;
+                  }
+                  if (p_ok && o_ok) {
+                    trace(tr, 1, 4 * pv_issued + 2);
+                    fence_proxy_async();
+                    tc_fence_after();
+                    issue_pv(tmem + kTmemO, sK0 + st * kStageBytes, idesc_pv, j == ja);
+                    trace(tr, 1, 4 * pv_issued + 3);
+                    tc_commit(smem_addr(&ctl.kv_empty[st]));
+                    tc_commit(smem_addr(&ctl.pv_done[pv_issued & 1]));
+                    if (j + 1 == jb) tc_commit(smem_addr(&ctl.o_full));
+                    ++pv_issued;
+                    need_pv = false;
+                    progress = true;
+                  }
+                }
               }
             }
             if (!progress) {
