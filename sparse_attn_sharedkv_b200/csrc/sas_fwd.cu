@@ -408,6 +408,38 @@ __device__ __forceinline__ int row_tiles(const Row& rv) {
   return (rv.slots + kTileKeys - 1) / kTileKeys;
 }
 
+// Walks the (row, tile) units of a worker span in plan order, skipping rows
+// without key tiles.  first / last: the tile opens / closes its (row, piece).
+struct TileCursor {
+  RowStream rs;
+  Span span;
+  int r, j, ja, jb;
+  bool valid;
+  __device__ __forceinline__ TileCursor(const int* rows, const Span& sp)
+      : rs(rows, sp.r0, sp.r1), span(sp), r(sp.r0 - 1), j(0), ja(0), jb(0), valid(false) {
+    next_row();
+  }
+  __device__ __forceinline__ void next_row() {
+    valid = false;
+    while (span.r0 >= 0 && ++r <= span.r1) {
+      const Row rv = rs.take(r);
+      const int tiles = row_tiles(rv);
+      ja = (r == span.r0) ? span.t0 : 0;
+      jb = (r == span.r1) ? span.t1 : (tiles > 0 ? tiles : 1);
+      if (tiles > 0 && ja < jb) {
+        j = ja;
+        valid = true;
+        return;
+      }
+    }
+  }
+  __device__ __forceinline__ void advance() {
+    if (++j >= jb) next_row();
+  }
+  __device__ __forceinline__ bool first() const { return j == ja; }
+  __device__ __forceinline__ bool last() const { return j + 1 == jb; }
+};
+
 // Source of one key slot: pool 0 = window cache (ori_kv), 1 = compressed
 // cache (cmp_kv), -1 = masked slot; row = block * block_size + offset in that
 // pool, or -1 for an attended position whose page is unmapped (zero row).
@@ -907,119 +939,129 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Barrier parities as bits: kv_full (bit = stage), s_empty (bit = S buffer).
       uint32_t kv_full_par = 0u, s_empty_par = 3u;
       uint32_t q_full_par = 0u, p_full_par = 0u, o_free_par = 1u;
-      int stage = 0, sbuf = 0, pv_issued = 0, qk_issued = 0, q_seen = 0;
+      int pv_issued = 0, qk_issued = 0, q_seen = 0;
       const bool pv_first = args.scenario == SAS_SCENARIO_SCFA;
       bool ok = true;
-
-      RowStream rs(rows, span.r0, span.r1);
-      for (int r = span.r0; ok && span.r0 >= 0 && r <= span.r1; ++r) {
-        const Row rv = rs.take(r);
-        const int tiles = row_tiles(rv);
-        const int ja = (r == span.r0) ? span.t0 : 0;
-        const int jb = (r == span.r1) ? span.t1 : (tiles > 0 ? tiles : 1);
-        if (tiles == 0 || ja >= jb) continue;
-        if (!wait_bar(&ctl, &ctl.q_full, q_full_par, err, 22)) { ok = false; break; }
+      // The worker's tiles form one stream across rows: QK(t+1) may open the
+      // next row (it then waits for that row's Q) while PV(t) is pending, so
+      // a row boundary does not drain the pipe.  Tile t uses K stage t % 2
+      // and S buffer t % 2.
+      TileCursor qc(rows, span), pc(rows, span);
+      int qstage = 0, pstage = 0;
+      // QK of the first tile, blocking.
+      if (qc.valid) {
+        if (!wait_bar(&ctl, &ctl.q_full, q_full_par, err, 22)) ok = false;
         q_full_par ^= 1u;
         trace(tr, 3, 6144 + q_seen++);
-        if (!wait_bar(&ctl, &ctl.s_empty[sbuf], (s_empty_par >> sbuf) & 1u, err, 21)) { ok = false; break; }
-        s_empty_par ^= 1u << sbuf;
         trace(tr, 1, 4 * qk_issued);
         for (int cg = 0; cg < kChunkGroups && ok; ++cg) {
-          if (!wait_bar(&ctl, &ctl.kv_full[stage][cg], (kv_full_par >> stage) & 1u, err, 20)) {
+          if (!wait_bar(&ctl, &ctl.kv_full[0][cg], 0u, err, 20)) {
             ok = false;
             break;
           }
           fence_proxy_async();
           tc_fence_after();
-          issue_qk_group<nchunks>(tmem + kTmemS + 128u * sbuf, sQ, sK0 + stage * kStageBytes,
-                                  idesc_qk, cg);
+          issue_qk_group<nchunks>(tmem + kTmemS, sQ, sK0, idesc_qk, cg);
         }
-        if (!ok) break;
-        kv_full_par ^= 1u << stage;
-        trace(tr, 1, 4 * qk_issued + 1);
-        ++qk_issued;
-        tc_commit(smem_addr(&ctl.s_full[sbuf]));
-        if (jb - ja == 1) tc_commit(smem_addr(&ctl.q_empty));
-        for (int j = ja; j < jb && ok; ++j) {
-          const int st = stage;
-          stage ^= 1;
-          sbuf ^= 1;
-          // Issue QK(j+1) and PV(j) in whichever order their inputs arrive
-          // (QK first when both are ready, so softmax(j+1) overlaps PV(j)).
-          bool need_qk = (j + 1 < jb), s_ok = false;
-          int qg = 0;  // chunk groups of QK(j+1) issued
-          bool need_pv = true, p_ok = false, o_ok = (j != ja);
-          long long t0 = clock64();
-          // QK(j+1) goes one chunk group at a time, as the groups land.  Top-k
-          // tiles (gathered row by row) issue PV(j) first, since it releases
-          // the stage the gather of tile j + 2 waits for; window / compressed
-          // runs (fast box loads) issue landed QK groups first, so softmax(j+1)
-          // overlaps PV(j).
-          while (need_qk || need_pv) {
-            bool progress = false;
-            for (int pass = 0; pass < 2; ++pass) {
-              if ((pass == 0) != pv_first) {
-                if (need_qk) {
-                  if (!s_ok && mbar_test(smem_addr(&ctl.s_empty[sbuf]), (s_empty_par >> sbuf) & 1u)) {
-                    s_ok = true;
-                    s_empty_par ^= 1u << sbuf;
-                    trace(tr, 1, 4 * qk_issued);
-                  }
-                  if (s_ok && qg < kChunkGroups &&
-                      mbar_test(smem_addr(&ctl.kv_full[stage][qg]), (kv_full_par >> stage) & 1u)) {
-                    fence_proxy_async();
-                    tc_fence_after();
-                    issue_qk_group<nchunks>(tmem + kTmemS + 128u * sbuf, sQ,
-                                            sK0 + stage * kStageBytes, idesc_qk, qg);
-                    ++qg;
-                    progress = true;
-                  }
-                  if (qg == kChunkGroups) {
-                    kv_full_par ^= 1u << stage;
-                    trace(tr, 1, 4 * qk_issued + 1);
-                    ++qk_issued;
-                    tc_commit(smem_addr(&ctl.s_full[sbuf]));
-                    if (j + 2 == jb) tc_commit(smem_addr(&ctl.q_empty));
-                    need_qk = false;
-                  }
+        if (ok) {
+          kv_full_par ^= 1u;
+          s_empty_par ^= 1u;  // buffer 0 was free
+          trace(tr, 1, 4 * qk_issued + 1);
+          ++qk_issued;
+          tc_commit(smem_addr(&ctl.s_full[0]));
+          if (qc.last()) tc_commit(smem_addr(&ctl.q_empty));
+          qc.advance();
+          qstage = 1;
+        }
+      }
+      while (ok && pc.valid) {
+        // Pending: PV of tile pc (stage pstage) and QK of tile qc (stage
+        // qstage, S buffer qstage), if any.
+        bool need_qk = qc.valid, need_pv = true;
+        bool q_ok = !qc.valid || !qc.first(), s_ok = false;
+        int qg = 0;  // chunk groups of the QK issued
+        bool p_ok = false, o_ok = !pc.first();
+        long long t0 = clock64();
+        // QK goes one chunk group at a time, as the groups land.  Top-k tiles
+        // (gathered row by row) issue PV first, since it releases the stage
+        // that the gather two tiles ahead waits for; window / compressed runs
+        // (fast box loads) issue landed QK groups first, so the next softmax
+        // overlaps PV.
+        while (need_qk || need_pv) {
+          bool progress = false;
+          for (int pass = 0; pass < 2; ++pass) {
+            if ((pass == 0) != pv_first) {
+              if (need_qk) {
+                if (!q_ok && mbar_test(smem_addr(&ctl.q_full), q_full_par)) {
+                  q_ok = true;
+                  q_full_par ^= 1u;
+                  trace(tr, 3, 6144 + q_seen++);
                 }
-              } else {
-                if (need_pv && (pv_first || !progress)) {
-                  if (!p_ok && mbar_test(smem_addr(&ctl.p_full), p_full_par)) {
-                    p_ok = true;
-                    p_full_par ^= 1u;
-                  }
-                  if (!o_ok && mbar_test(smem_addr(&ctl.o_free), o_free_par)) {
-                    o_ok = true;
-                    o_free_par ^= 1u;
-                  }
-                  if (p_ok && o_ok) {
-                    trace(tr, 1, 4 * pv_issued + 2);
-                    fence_proxy_async();
-                    tc_fence_after();
-                    issue_pv(tmem + kTmemO, sK0 + st * kStageBytes, idesc_pv, j == ja);
-                    trace(tr, 1, 4 * pv_issued + 3);
-                    tc_commit(smem_addr(&ctl.kv_empty[st]));
-                    tc_commit(smem_addr(&ctl.pv_done[pv_issued & 1]));
-                    if (j + 1 == jb) tc_commit(smem_addr(&ctl.o_full));
-                    ++pv_issued;
-                    need_pv = false;
-                    progress = true;
-                  }
+                if (q_ok && !s_ok &&
+                    mbar_test(smem_addr(&ctl.s_empty[qstage]), (s_empty_par >> qstage) & 1u)) {
+                  s_ok = true;
+                  s_empty_par ^= 1u << qstage;
+                  trace(tr, 1, 4 * qk_issued);
+                }
+                if (s_ok && qg < kChunkGroups &&
+                    mbar_test(smem_addr(&ctl.kv_full[qstage][qg]), (kv_full_par >> qstage) & 1u)) {
+                  fence_proxy_async();
+                  tc_fence_after();
+                  issue_qk_group<nchunks>(tmem + kTmemS + 128u * qstage, sQ,
+                                          sK0 + qstage * kStageBytes, idesc_qk, qg);
+                  ++qg;
+                  progress = true;
+                }
+                if (qg == kChunkGroups) {
+                  kv_full_par ^= 1u << qstage;
+                  trace(tr, 1, 4 * qk_issued + 1);
+                  ++qk_issued;
+                  tc_commit(smem_addr(&ctl.s_full[qstage]));
+                  if (qc.last()) tc_commit(smem_addr(&ctl.q_empty));
+                  need_qk = false;
                 }
               }
-            }
-            if (!progress) {
-              if (ctl.abort) { ok = false; break; }
-              if (clock64() - t0 > kWaitCycles) {
-                record_error(err, SAS_ERR_DEVICE, 23, j);
-                ctl.abort = 1;
-                ok = false;
-                break;
+            } else if (need_pv && (pv_first || !progress)) {
+              if (!p_ok && mbar_test(smem_addr(&ctl.p_full), p_full_par)) {
+                p_ok = true;
+                p_full_par ^= 1u;
+              }
+              if (!o_ok && mbar_test(smem_addr(&ctl.o_free), o_free_par)) {
+                o_ok = true;
+                o_free_par ^= 1u;
+              }
+              if (p_ok && o_ok) {
+                trace(tr, 1, 4 * pv_issued + 2);
+                fence_proxy_async();
+                tc_fence_after();
+                issue_pv(tmem + kTmemO, sK0 + pstage * kStageBytes, idesc_pv, pc.first());
+                trace(tr, 1, 4 * pv_issued + 3);
+                tc_commit(smem_addr(&ctl.kv_empty[pstage]));
+                tc_commit(smem_addr(&ctl.pv_done[pv_issued & 1]));
+                if (pc.last()) tc_commit(smem_addr(&ctl.o_full));
+                ++pv_issued;
+                need_pv = false;
+                progress = true;
               }
             }
           }
+          if (!progress) {
+            if (ctl.abort) { ok = false; break; }
+            if (clock64() - t0 > kWaitCycles) {
+              record_error(err, SAS_ERR_DEVICE, 23, pv_issued);
+              ctl.abort = 1;
+              ok = false;
+              break;
+            }
+          }
         }
+        if (!ok) break;
+        if (qc.valid) {
+          qc.advance();
+          qstage ^= 1;
+        }
+        pc.advance();
+        pstage ^= 1;
       }
       // Drain: the commit arrives once every MMA issued above has finished,
       // so TMEM is never released under an in-flight MMA (also on abort).
