@@ -20,6 +20,12 @@
  *   sas_plan_size / sas_plan
  *       the B200 work split that takes the place of the 24/36-core metadata
  *       table for 148 SMs (split-KV pieces + combine bookkeeping).
+ *   sas_kv_append
+ *       the paged-cache writer that precedes the path: appends new key rows
+ *       into a [blocks, block_size, 1, D] pool through its block table, in the
+ *       layout of the reference's generators golden.py:315-360 (the inverse of
+ *       unpack_paged_kv, golden.py:247-268).  The reference has no device
+ *       writer: its tests build the caches on the host.
  *   sas_error_string / sas_version
  *       error reporting in place of the reference's Python asserts
  *       (api.py:187-191, 279-282).
@@ -189,6 +195,24 @@ int sas_combine(const int32_t* row_token, const int32_t* row_pieces,
                 const int32_t* partial_base, int32_t num_rows, const float* o_partial,
                 const float* lse_partial, int32_t num_heads, int32_t head_dim_v, int32_t dtype,
                 void* out, float* lse, void* stream);
+
+/* ---- paged-cache writer ---- */
+
+/* Append new key rows into a paged cache, in place: batch b writes its rows
+ * rows[cu_new[b] .. cu_new[b+1]) at logical positions start_pos[b] + i, i.e.
+ * at pool[block_table[b, p / block_size], p % block_size].  pool [device]
+ * [num_blocks, block_size, 1, row_bytes / 2]; rows [device] [total_new,
+ * row_bytes / 2] (any 16-bit dtype: the writer copies bytes); block_table
+ * [device] [batch, table_len] int32; cu_new [device] [batch + 1] int32;
+ * start_pos [device] [batch] int32 (usually the lengths before the append).
+ * row_bytes a multiple of 16, pool and rows 16-byte aligned.  A row whose
+ * position is past the table or whose page is -1 / outside the pool is
+ * skipped and recorded in the optional err word [device] int32[4] (site 50,
+ * detail = row index).  Stream-ordered, no allocation. */
+int sas_kv_append(void* pool, int32_t num_blocks, int32_t block_size, int32_t row_bytes,
+                  const int32_t* block_table, int32_t table_len, const void* rows,
+                  const int32_t* cu_new, const int32_t* start_pos, int32_t batch,
+                  int32_t total_new, int32_t* err, void* stream);
 
 /* ---- B200 work plan (host) ---- */
 

@@ -322,3 +322,37 @@ def count_keys(*, layout_q: str, cu_seqlens_q: Optional[Sequence[int]], B: int, 
                 else:
                     cmpk += max(cmp_threshold(akv, aq, s, cmp_ratio), 0)
     return {"tokens": tokens, "window_keys": win, "cmp_keys": cmpk, "keys": win + cmpk}
+
+
+# ---------------------------------------------------------------------------
+# Paged-cache writer (the step before the attention path).
+# ---------------------------------------------------------------------------
+
+def append_paged(pool: np.ndarray, block_table: np.ndarray, rows: np.ndarray,
+                 cu_new: Sequence[int], start_pos: Sequence[int]) -> List[int]:
+    """Write new key rows into a paged cache, in place.
+
+    The paged layout is the reference's (golden.py:315-360, inverse of
+    ``unpack_paged_kv``, golden.py:247-268): logical position ``p`` of batch
+    ``b`` lives at ``pool[block_table[b, p // bs], p % bs]``.  Batch ``b``
+    appends ``rows[cu_new[b]:cu_new[b+1]]`` at positions ``start_pos[b] + i``.
+    ``pool`` is ``[blocks, bs, D]`` (the N2 = 1 axis dropped), ``rows``
+    ``[T_new, D]``; any dtype (the writer copies bits).
+
+    Returns the indices of the new rows that could not be written (position
+    past the block table, or an unmapped / out-of-pool page); those rows are
+    skipped, as the CUDA writer does.
+    """
+    blocks, bs = pool.shape[0], pool.shape[1]
+    table_len = block_table.shape[1]
+    bad = []
+    for b in range(len(cu_new) - 1):
+        for i in range(int(cu_new[b]), int(cu_new[b + 1])):
+            pos = int(start_pos[b]) + (i - int(cu_new[b]))
+            lb = pos // bs
+            blk = int(block_table[b, lb]) if 0 <= lb < table_len else -1
+            if blk < 0 or blk >= blocks or pos < 0:
+                bad.append(i)
+                continue
+            pool[blk, pos % bs] = rows[i]
+    return bad

@@ -97,6 +97,9 @@ PROTOTYPES = {
                                   C.c_int32]),
     "sas_fwd_noalloc": (C.c_int, [C.POINTER(SasProblem), C.POINTER(SasFwdParams),
                                   C.c_void_p]),
+    "sas_kv_append": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
+                                C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32,
+                                C.c_int32, C.c_void_p, C.c_void_p]),
     "sas_combine": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p,
                               C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
                               C.c_void_p, C.c_void_p]),

@@ -19,8 +19,8 @@ LIB_DIR = os.path.join(PKG, "_lib")
 LIB = os.path.join(LIB_DIR, "libsas.so")
 INCLUDE = os.path.join(REPO, "include")
 
-SOURCES = ["sas_capi.cu", "sas_fwd.cu", "sas_combine.cu", "sas_noalloc.cu", "sas_plan.cpp",
-           "sas_metadata.cpp"]
+SOURCES = ["sas_capi.cu", "sas_fwd.cu", "sas_combine.cu", "sas_noalloc.cu", "sas_kvwrite.cu",
+           "sas_plan.cpp", "sas_metadata.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
