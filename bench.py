@@ -24,9 +24,11 @@ Printed JSON line (rank 0):
 own implementation cannot run here: it needs an Ascend NPU / TileLang-Ascend;
 its CPU golden cannot travel to the GPU box, so the oracle port stands in).
 
-Multi-GPU (torchrun, one rank per GPU): every rank processes its own copy of
-the workload (weak scaling, no collective in the step; the barrier and the
-max-over-ranks reduction of the timing are the only communication).
+Multi-GPU (torchrun, one rank per GPU): the global workload is N copies of
+the configuration's sequences, sharded one copy per rank (weak scaling; the
+step itself needs no collective).  The sharded call's one exchange, the
+all-gather of the output / LSE shards (sharding.gather_outputs, NCCL), is
+timed separately under ``allgather``.
 """
 
 from __future__ import annotations
@@ -386,12 +388,35 @@ def run_gpu(args):
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
     d2h = lse_host.numel() * lse_host.element_size()
 
+    # ---- N > 1: the one exchange of a sharded call, an all-gather of the
+    # output / LSE shards over NCCL (timed apart from `value`) ----
+    gather_ms, gather_bytes, gather_note = 0.0, 0, None
+    if ws > 1:
+        from sparse_attn_sharedkv_b200 import sharding as SH
+        out_t, lse_t = A.sparse_attn_sharedkv(q, return_softmax_lse=True, **kw)
+        n_units = out_t.shape[0]
+        gather_bytes = ws * (out_t.numel() * out_t.element_size() + lse_t.numel() * 4)
+        if gather_bytes <= (16 << 30):
+            plan = [(r * n_units, (r + 1) * n_units) for r in range(ws)]
+            args_g = (plan, rank, tuple(out_t.shape[1:]), tuple(lse_t.shape[1:]), out_t.dtype, dev)
+            SH.gather_outputs(out_t, lse_t, *args_g)  # warm-up
+            barrier()
+            g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            g0.record(stream)
+            SH.gather_outputs(out_t, lse_t, *args_g)
+            g1.record(stream)
+            barrier()
+            gather_ms = g0.elapsed_time(g1)
+        else:
+            gather_note = "skipped: gathered output above 16 GB per rank"
+        del out_t, lse_t
+
     # ---- max over ranks ----
-    vals = torch.tensor([total_ms, kern_ms, e2e_ms], dtype=torch.float64, device=dev)
+    vals = torch.tensor([total_ms, kern_ms, e2e_ms, gather_ms], dtype=torch.float64, device=dev)
     if ws > 1:
         import torch.distributed as dist
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    total_ms, kern_ms, e2e_ms = vals.tolist()
+    total_ms, kern_ms, e2e_ms, gather_ms = vals.tolist()
 
     if rank == 0:
         peaks, peak_src = load_peaks()
@@ -444,6 +469,11 @@ def run_gpu(args):
                          "tensor_tflops": flops / (kern_ms * 1e-3) / 1e12,
                          "hbm_gbs": nbytes_alg / (kern_ms * 1e-3) / 1e9},
             "cpu_baseline": cpu,
+            "allgather": (None if ws == 1 else
+                          {"ms": gather_ms, "bytes_gathered_per_rank": gather_bytes,
+                           "what": "NCCL all-gather of every rank's output and LSE shard "
+                                   "(the sharded call's one exchange); not part of value",
+                           "note": gather_note}),
             "clocks": clocks,
             "gpu_launches": launches_per_step * args.steps,
         }
