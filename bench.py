@@ -454,7 +454,8 @@ def run_gpu(args):
                 "hbm_gbs_per_gpu": nbytes_alg / (ms_step * 1e-3) / 1e9,
                 "l2": ("flushed between steps (256 MB write)" if in_l2
                        else "inputs larger than L2 (126 MB)"),
-                "parallelism": f"dp{ws} (independent copies per rank, weak scaling)",
+                "parallelism": (f"dp{ws}: one shard (a copy of the configuration's sequences) "
+                                f"per rank, weak scaling"),
                 "plan": {"workers": info.num_workers, "head_groups": info.head_groups,
                          "split_rows": info.num_split_rows, "tiles": int(info.total_tiles)},
             },
