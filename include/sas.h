@@ -20,6 +20,9 @@
  *   sas_plan_size / sas_plan
  *       the B200 work split that takes the place of the 24/36-core metadata
  *       table for 148 SMs (split-KV pieces + combine bookkeeping).
+ *   sas_fwd_workspace_size_device / sas_fwd_prepare_device
+ *       the same plan built on the GPU from device-resident lengths, in place
+ *       of the host reads api.py:210, 260, 336 (no host sync, graph-capturable).
  *   sas_kv_append
  *       the paged-cache writer that precedes the path: appends new key rows
  *       into a [blocks, block_size, 1, D] pool through its block table, in the
@@ -171,6 +174,22 @@ int sas_fwd_prepare(const SasProblem* prob, const SasFwdParams* params, void* wo
                     size_t workspace_bytes, void* stream, SasPlanInfo* info);
 int sas_fwd_execute(const SasProblem* prob, const SasFwdParams* params, const SasPlanInfo* info,
                     void* workspace, size_t workspace_bytes, void* stream, int32_t phases);
+
+/* Device-planned forward: the same as sas_fwd_prepare, except that
+ * prob->q_start, q_len and kv_len are DEVICE pointers ([device] int32[B]) and
+ * the work plan is built on the GPU by one small kernel, so the call reads no
+ * length on the host (the reference syncs on them, api.py:210, 260, 336) and
+ * the prepare + execute launches can be recorded in a CUDA graph and replayed
+ * with new lengths of the same shapes.  q_start must be the prefix sums of
+ * q_len (TND) or b * max_q_len (BSND).  The plan is the host planner's
+ * (same rows, workers, split rows); its sections are sized for the worst
+ * case (info->num_split_rows / num_partials are upper bounds), so the
+ * workspace comes from sas_fwd_workspace_size_device.  Invalid lengths are
+ * reported in params->err (site 60) and leave the call without work.
+ * Then sas_fwd_execute as usual. */
+int sas_fwd_workspace_size_device(const SasProblem* prob, int32_t num_sms, size_t* bytes);
+int sas_fwd_prepare_device(const SasProblem* prob, const SasFwdParams* params, void* workspace,
+                           size_t workspace_bytes, void* stream, SasPlanInfo* info);
 
 /* Forward without a caller workspace, for callers that cannot allocate
  * device memory (an arena planned ahead of time, an allocator frozen during a

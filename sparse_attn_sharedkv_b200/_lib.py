@@ -95,6 +95,11 @@ PROTOTYPES = {
     "sas_fwd_execute": (C.c_int, [C.POINTER(SasProblem), C.POINTER(SasFwdParams),
                                   C.POINTER(SasPlanInfo), C.c_void_p, C.c_size_t, C.c_void_p,
                                   C.c_int32]),
+    "sas_fwd_workspace_size_device": (C.c_int, [C.POINTER(SasProblem), C.c_int32,
+                                                C.POINTER(C.c_size_t)]),
+    "sas_fwd_prepare_device": (C.c_int, [C.POINTER(SasProblem), C.POINTER(SasFwdParams),
+                                         C.c_void_p, C.c_size_t, C.c_void_p,
+                                         C.POINTER(SasPlanInfo)]),
     "sas_fwd_noalloc": (C.c_int, [C.POINTER(SasProblem), C.POINTER(SasFwdParams),
                                   C.c_void_p]),
     "sas_kv_append": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,

@@ -28,6 +28,11 @@ reference behaviour where the reference supports the shape):
 * ``ori_win_left = -1``: empty window (pure top-k attention when combined
   with SCFA, ``cmp_ratio = 1`` and ``cmp_kv`` the same cache).
 * ``num_sms``: number of persistent workers (default: all SMs).
+* ``device_plan``: keep ``cu_seqlens_q`` / ``seqused_kv`` on the device and
+  build the work plan on the GPU (``sas_fwd_prepare_device``): the call reads
+  no length on the host (the reference syncs on them, api.py:210, 260, 336),
+  so it can be recorded in a CUDA graph and replayed with new lengths of the
+  same shapes.
 
 ``metadata`` (the SparseAttnSharedkvMetadata table) and ``core_num`` are
 accepted and validated for API parity; like the reference kernels
@@ -49,7 +54,12 @@ from . import _lib
 DEFAULT_CORE_NUM = 24  # the reference's AIC count default (kernel.py:70)
 SAS_META_SIZE = _lib.SAS_META_SIZE
 
-_CHECK_DEVICE = os.environ.get("SAS_CHECK_DEVICE_ERRORS", "0") == "1"
+def _check_device_errors() -> bool:
+    """SAS_CHECK_DEVICE_ERRORS=1: give each call a device error word and raise
+    if the kernel recorded an error (costs a sync).  Read per call; off while
+    a CUDA graph is being captured (the read-back cannot be recorded)."""
+    return (os.environ.get("SAS_CHECK_DEVICE_ERRORS", "0") == "1"
+            and not torch.cuda.is_current_stream_capturing())
 
 # Plans (host schedule uploaded into a device workspace) are reused across
 # calls with the same lengths and shapes, as a serving step reuses one
@@ -95,12 +105,16 @@ class CallArgs:
 def build_call(q: torch.Tensor, *, ori_kv, cmp_kv=None, cmp_sparse_indices=None,
                ori_block_table, cmp_block_table=None, cu_seqlens_q=None, seqused_kv,
                sinks, softmax_scale, cmp_ratio=None, ori_win_left=127, layout_q="TND",
-               topk_cmp=None, head_dim_v=None, num_sms=None, err=None) -> CallArgs:
+               topk_cmp=None, head_dim_v=None, num_sms=None, err=None,
+               device_plan=False) -> CallArgs:
     """Validate the reference-style arguments and build the C-ABI structs.
 
     Mirrors api.py:196-366 (scenario resolution, TND/BSND flattening, K
     resolution, shape checks); allocates the flat ``out [T, N1, d_v]`` and
-    ``lse [T, N1]`` that ``sas_fwd`` writes.
+    ``lse [T, N1]`` that ``sas_fwd`` writes.  With ``device_plan`` the
+    per-batch lengths stay on the device and ``SasProblem`` carries device
+    pointers (for ``sas_fwd_prepare_device``): the call reads no length on the
+    host.
     """
     dtype = q.dtype
     dcode = _dtype_code(dtype)
@@ -119,14 +133,21 @@ def build_call(q: torch.Tensor, *, ori_kv, cmp_kv=None, cmp_sparse_indices=None,
     # ---- flat [T, N1, D] view + per-batch offsets (api.py:204-240) ----
     if layout_q == "TND":
         _require(cu_seqlens_q is not None, "cu_seqlens_q is required for TND")
-        cu = cu_seqlens_q.to(torch.int64).cpu().tolist()
-        B = len(cu) - 1
         T1, N1, D = q.shape
         total = T1
         q_flat = q
-        q_start = cu[:-1]
-        q_len = [cu[i + 1] - cu[i] for i in range(B)]
-        S_max = max(q_len) if q_len else 0
+        if device_plan:
+            B = cu_seqlens_q.numel() - 1
+            cu_d = cu_seqlens_q.to(device=dev, dtype=torch.int32)
+            q_start = cu_d[:-1].contiguous()
+            q_len = (cu_d[1:] - cu_d[:-1]).contiguous()
+            S_max = 0
+        else:
+            cu = cu_seqlens_q.to(torch.int64).cpu().tolist()
+            B = len(cu) - 1
+            q_start = cu[:-1]
+            q_len = [cu[i + 1] - cu[i] for i in range(B)]
+            S_max = max(q_len) if q_len else 0
         idx_flat = None
         if scenario == _lib.SCENARIO_SCFA:
             idx_flat = cmp_sparse_indices
@@ -136,11 +157,20 @@ def build_call(q: torch.Tensor, *, ori_kv, cmp_kv=None, cmp_sparse_indices=None,
         B, S_max, N1, D = q.shape
         total = B * S_max
         q_flat = q.reshape(total, N1, D)
-        q_start = [b * S_max for b in range(B)]
-        q_len = [S_max] * B
-        if cu_seqlens_q is not None:
-            cu = cu_seqlens_q.to(torch.int64).cpu().tolist()
-            q_len = [cu[i + 1] - cu[i] for i in range(B)]
+        if device_plan:
+            q_start = torch.arange(0, max(total, 1), max(S_max, 1), dtype=torch.int32,
+                                   device=dev)[:B].contiguous()
+            if cu_seqlens_q is not None:
+                cu_d = cu_seqlens_q.to(device=dev, dtype=torch.int32)
+                q_len = (cu_d[1:] - cu_d[:-1]).contiguous()
+            else:
+                q_len = torch.full((B,), S_max, dtype=torch.int32, device=dev)
+        else:
+            q_start = [b * S_max for b in range(B)]
+            q_len = [S_max] * B
+            if cu_seqlens_q is not None:
+                cu = cu_seqlens_q.to(torch.int64).cpu().tolist()
+                q_len = [cu[i + 1] - cu[i] for i in range(B)]
         idx_flat = None
         if scenario == _lib.SCENARIO_SCFA:
             ci = cmp_sparse_indices
@@ -148,9 +178,11 @@ def build_call(q: torch.Tensor, *, ori_kv, cmp_kv=None, cmp_sparse_indices=None,
     else:
         raise AssertionError(f"unsupported layout_q={layout_q!r}")
 
-    kv_len = seqused_kv.to(torch.int64).cpu().tolist()
-    _require(len(kv_len) >= B, "seqused_kv must have one entry per batch")
-    kv_len = kv_len[:B]
+    _require(seqused_kv.numel() >= B, "seqused_kv must have one entry per batch")
+    if device_plan:
+        kv_len = seqused_kv.reshape(-1)[:B].to(device=dev, dtype=torch.int32).contiguous()
+    else:
+        kv_len = seqused_kv.to(torch.int64).cpu().tolist()[:B]
 
     if scenario == _lib.SCENARIO_SCFA:
         N2 = idx_flat.shape[1]
@@ -197,10 +229,16 @@ def build_call(q: torch.Tensor, *, ori_kv, cmp_kv=None, cmp_sparse_indices=None,
     prob.layout_q = _lib.LAYOUTS[layout_q]
     prob.max_q_len = S_max
     prob.total_tokens = total
-    a_start, a_len, a_kv = _i32_array(q_start), _i32_array(q_len), _i32_array(kv_len)
-    prob.q_start = C.cast(a_start, C.POINTER(C.c_int32))
-    prob.q_len = C.cast(a_len, C.POINTER(C.c_int32))
-    prob.kv_len = C.cast(a_kv, C.POINTER(C.c_int32))
+    if device_plan:
+        a_start, a_len, a_kv = q_start, q_len, kv_len  # device int32 tensors
+        prob.q_start = C.cast(C.c_void_p(q_start.data_ptr()), C.POINTER(C.c_int32))
+        prob.q_len = C.cast(C.c_void_p(q_len.data_ptr()), C.POINTER(C.c_int32))
+        prob.kv_len = C.cast(C.c_void_p(kv_len.data_ptr()), C.POINTER(C.c_int32))
+    else:
+        a_start, a_len, a_kv = _i32_array(q_start), _i32_array(q_len), _i32_array(kv_len)
+        prob.q_start = C.cast(a_start, C.POINTER(C.c_int32))
+        prob.q_len = C.cast(a_len, C.POINTER(C.c_int32))
+        prob.kv_len = C.cast(a_kv, C.POINTER(C.c_int32))
     prob.num_heads = N1
     prob.scenario = scenario
     prob.ori_win_left = int(ori_win_left)
@@ -228,10 +266,12 @@ def build_call(q: torch.Tensor, *, ori_kv, cmp_kv=None, cmp_sparse_indices=None,
         fp.cmp_block_size, fp.cmp_num_blocks = cmp.shape[1], cmp.shape[0]
         fp.cmp_table_len = cmp_bt.shape[1]
     fp.num_sms = int(num_sms or 0)
+    lengths_key = (("device", B) if device_plan
+                   else (tuple(q_start), tuple(q_len), tuple(kv_len)))
     return CallArgs(prob=prob, fp=fp, out=out, lse=lse, total=total, device=dev,
-                    plan_key=(layout_q, tuple(q_start), tuple(q_len), tuple(kv_len), N1,
-                              scenario, int(ori_win_left), ratio, int(K), fp.num_sms, total,
-                              S_max),
+                    device_plan=bool(device_plan),
+                    plan_key=(layout_q, lengths_key, N1, scenario, int(ori_win_left), ratio,
+                              int(K), fp.num_sms, total, S_max),
                     keep=(q_flat, ori, ori_bt, cmp, cmp_bt, idx, snk, err, a_start, a_len,
                           a_kv))
 
@@ -247,6 +287,31 @@ def _forward(q: torch.Tensor, **kw):
     with torch.cuda.device(dev):
         stream = torch.cuda.current_stream(dev).cuda_stream
         key = (dev.index, stream) + call.plan_key
+        if call.device_plan:
+            # The plan depends on device-resident lengths: rebuilt on the GPU
+            # every call (one small kernel); the workspace is cached per shape.
+            hit = _PLAN_CACHE.get(key)
+            if hit is None:
+                ws_bytes = C.c_size_t(0)
+                _lib.check("sas_fwd_workspace_size_device",
+                           L.sas_fwd_workspace_size_device(C.byref(prob), fp.num_sms,
+                                                           C.byref(ws_bytes)))
+                ws = torch.empty(max(ws_bytes.value, 256), dtype=torch.uint8, device=dev)
+                hit = (ws, ws_bytes.value, None)
+                _PLAN_CACHE[key] = hit
+                while len(_PLAN_CACHE) > _PLAN_CACHE_SIZE:
+                    _PLAN_CACHE.popitem(last=False)
+            ws, nbytes, _ = hit
+            info = _lib.SasPlanInfo()
+            _lib.check("sas_fwd_prepare_device",
+                       L.sas_fwd_prepare_device(C.byref(prob), C.byref(fp), ws.data_ptr(), nbytes,
+                                                C.c_void_p(stream), C.byref(info)))
+            last_plan_info = info
+            _lib.check("sas_fwd_execute",
+                       L.sas_fwd_execute(C.byref(prob), C.byref(fp), C.byref(info),
+                                         ws.data_ptr(), nbytes, C.c_void_p(stream),
+                                         _lib.PHASE_ALL))
+            return out, lse
         hit = _PLAN_CACHE.get(key)
         if hit is None:
             ws_bytes = C.c_size_t(0)
@@ -297,6 +362,7 @@ def sparse_attn_sharedkv(
     topk_cmp: Optional[int] = None,
     head_dim_v: Optional[int] = None,
     num_sms: Optional[int] = None,
+    device_plan: bool = False,
 ) -> Union[torch.Tensor, Tuple[torch.Tensor, torch.Tensor]]:
     """Sparse shared-KV attention forward; see the module docstring."""
     del seqused_q, core_num  # API parity (api.py:186); the B200 plan uses all SMs
@@ -309,14 +375,15 @@ def sparse_attn_sharedkv(
         _require(metadata.numel() == SAS_META_SIZE,
                  f"metadata must have {SAS_META_SIZE} int32 entries (got {metadata.numel()})")
     err = None
-    if _CHECK_DEVICE:
+    if _check_device_errors():
         err = torch.zeros(4, dtype=torch.int32, device=q.device)
     out_flat, lse_flat = _forward(
         q, ori_kv=ori_kv, cmp_kv=cmp_kv, cmp_sparse_indices=cmp_sparse_indices,
         ori_block_table=ori_block_table, cmp_block_table=cmp_block_table,
         cu_seqlens_q=cu_seqlens_q, seqused_kv=seqused_kv, sinks=sinks,
         softmax_scale=softmax_scale, cmp_ratio=cmp_ratio, ori_win_left=ori_win_left,
-        layout_q=layout_q, topk_cmp=topk_cmp, head_dim_v=head_dim_v, num_sms=num_sms, err=err)
+        layout_q=layout_q, topk_cmp=topk_cmp, head_dim_v=head_dim_v, num_sms=num_sms, err=err,
+        device_plan=device_plan)
     if err is not None:
         e = err.tolist()
         if e[0] != 0:

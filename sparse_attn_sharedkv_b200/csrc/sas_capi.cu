@@ -108,6 +108,42 @@ extern "C" int sas_fwd_prepare(const SasProblem* prob, const SasFwdParams* param
   return SAS_OK;
 }
 
+extern "C" int sas_fwd_workspace_size_device(const SasProblem* prob, int32_t num_sms,
+                                             size_t* bytes) {
+  if (!prob || !bytes) return SAS_ERR_INVALID;
+  const int sms = resolve_sms(num_sms);
+  if (sms <= 0) return SAS_ERR_CUDA;
+  SasPlanInfo info;
+  int rc = sas::plan_dev_info(*prob, sms, &info);
+  if (rc != SAS_OK) return rc;
+  *bytes = layout_for(info, prob->num_heads, 512).total;
+  return SAS_OK;
+}
+
+extern "C" int sas_fwd_prepare_device(const SasProblem* prob, const SasFwdParams* params,
+                                      void* workspace, size_t workspace_bytes,
+                                      void* stream_ptr, SasPlanInfo* info_out) {
+  if (!prob || !params || !info_out) return SAS_ERR_INVALID;
+  int rc = validate(*prob, *params);
+  if (rc != SAS_OK) return rc;
+  if (!prob->q_start || !prob->q_len || !prob->kv_len) return SAS_ERR_INVALID;
+  const int sms = resolve_sms(params->num_sms);
+  if (sms <= 0) return SAS_ERR_CUDA;
+  SasPlanInfo info;
+  rc = sas::plan_dev_info(*prob, sms, &info);
+  if (rc != SAS_OK) return rc;
+  *info_out = info;
+  if (info.num_rows == 0) return SAS_OK;
+  const WorkspaceLayout wl = layout_for(info, prob->num_heads, params->head_dim_v);
+  if (workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & (kAlign - 1)) != 0 ||
+      workspace_bytes < wl.total)
+    return SAS_ERR_WORKSPACE;
+  return sas::plan_dev_launch(*prob, info,
+                              reinterpret_cast<int32_t*>(static_cast<char*>(workspace) +
+                                                         wl.plan_off),
+                              params->err, reinterpret_cast<cudaStream_t>(stream_ptr));
+}
+
 extern "C" int sas_fwd_execute(const SasProblem* prob, const SasFwdParams* params,
                                const SasPlanInfo* info_ptr, void* workspace,
                                size_t workspace_bytes, void* stream_ptr, int32_t phases) {

@@ -40,6 +40,9 @@ __global__ void __launch_bounds__(32 * kHeadsPerBlock)
   const int token = __ldg(row_token + (size_t)row * stride);
   const int pieces = __ldg(row_pieces + (size_t)row * stride);
   const int base = __ldg(row_base + (size_t)row * stride);
+  // Unused entries of a device-built plan's split section (sized for the
+  // worst case) carry no pieces.
+  if (pieces <= 0) return;
 
   // Max of the piece LSEs.
   float mx = -INFINITY;

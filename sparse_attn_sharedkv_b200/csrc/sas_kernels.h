@@ -46,6 +46,9 @@ int launch_combine(const int32_t* row_token, const int32_t* row_pieces, const in
                    int stride, int n, const float* o_partial, const float* lse_partial, int num_heads,
                    int head_dim_v, int dtype, void* out, float* lse, cudaStream_t stream);
 
+int plan_dev_info(const SasProblem& p, int32_t num_sms, SasPlanInfo* info);
+int plan_dev_launch(const SasProblem& p, const SasPlanInfo& info, int32_t* dplan, int32_t* err,
+                    cudaStream_t stream);
 int plan_build(const SasProblem& p, int32_t num_sms, std::vector<int32_t>* plan,
                SasPlanInfo* info);
 

@@ -11,14 +11,12 @@ scenarios HCA (dense, scenario 2) and CSA (top-k, scenario 3)
 
 from __future__ import annotations
 
-import os
 from typing import Optional, Tuple, Union
 
 import torch
 
-from .api import DEFAULT_CORE_NUM, _forward, _require, _restore_layout
+from .api import DEFAULT_CORE_NUM, _check_device_errors, _forward, _require, _restore_layout
 
-_CHECK_DEVICE = os.environ.get("SAS_CHECK_DEVICE_ERRORS", "0") == "1"
 
 
 def sparse_flash_mla(
@@ -54,7 +52,7 @@ def sparse_flash_mla(
     _require(ori_win_right == 0, "only ori_win_right=0 supported")
     _require(layout_kv == "PA_ND", "only layout_kv=PA_ND supported")
     _require(layout_q in ("TND", "BSND"), f"unsupported layout_q={layout_q!r}")
-    err = torch.zeros(4, dtype=torch.int32, device=q.device) if _CHECK_DEVICE else None
+    err = torch.zeros(4, dtype=torch.int32, device=q.device) if _check_device_errors() else None
     out_flat, lse_flat = _forward(
         q, ori_kv=ori_kv, cmp_kv=cmp_kv, cmp_sparse_indices=cmp_sparse_indices,
         ori_block_table=ori_block_table, cmp_block_table=cmp_block_table,
