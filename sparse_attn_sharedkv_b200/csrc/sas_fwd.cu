@@ -350,8 +350,11 @@ struct RowStream {
   }
 };
 
-// Diagnostic clock trace of CTA 0: 4 regions of 8192 entries (producer, MMA,
-// softmax per tile, epilogue per row).
+// Diagnostic clock trace of one CTA (FwdArgs::trace_cta), compiled only into
+// the kernel instances launched with a trace buffer: 4 regions of 8192
+// entries: producer, MMA and softmax events per tile; in region 3 the
+// epilogue per row (from 0), the chunk-group landings seen by the MMA issuer
+// (from 2048), Q load issues (from 4096) and Q arrivals (from 6144).
 constexpr int kTraceRegion = 8192;
 __device__ __forceinline__ void trace(long long* tr, int region, int idx) {
   if (tr != nullptr && idx >= 0 && idx < kTraceRegion)
@@ -719,7 +722,7 @@ __device__ __forceinline__ void prefetch_rows(const FwdArgs& a, const SlotSrc& s
 // The kernel.
 // ---------------------------------------------------------------------------
 
-template <bool kBf16, int kChunks>
+template <bool kBf16, int kChunks, bool kTrace>
 __global__ void __launch_bounds__(kThreads, 1)
     sas_fwd_kernel(const FwdArgs args, const __grid_constant__ CUtensorMap tm_q,
                    const __grid_constant__ CUtensorMap tm_ori,
@@ -738,7 +741,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int* rows = plan + plan[H_ROWS_OFF];
   constexpr int nchunks = kChunks;  // d_qk / 64
   int* err = args.err;
-  long long* tr = ((int)blockIdx.x == args.trace_cta) ? args.trace : nullptr;
+  long long* tr = (kTrace && (int)blockIdx.x == args.trace_cta) ? args.trace : nullptr;
 
   // 1024-byte aligned tile area.
   const uint32_t raw = smem_addr(smem_raw);
@@ -940,7 +943,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t kv_full_par = 0u, s_empty_par = 3u;
       uint32_t q_full_par = 0u, p_full_par = 0u, o_free_par = 1u;
       int pv_issued = 0, qk_issued = 0, q_seen = 0;
-      const bool pv_first = args.scenario == SAS_SCENARIO_SCFA;
       bool ok = true;
       // The worker's tiles form one stream across rows: QK(t+1) may open the
       // next row (it then waits for that row's Q) while PV(t) is pending, so
@@ -982,15 +984,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         int qg = 0;  // chunk groups of the QK issued
         bool p_ok = false, o_ok = !pc.first();
         long long t0 = clock64();
-        // QK goes one chunk group at a time, as the groups land.  Top-k tiles
-        // (gathered row by row) issue PV first, since it releases the stage
-        // that the gather two tiles ahead waits for; window / compressed runs
-        // (fast box loads) issue landed QK groups first, so the next softmax
-        // overlaps PV.
+        // PV goes first whenever its P is in: it releases the K stage that
+        // the load two tiles ahead waits for, which is the longer chain
+        // (issuing the next QK first delayed the stage by the whole QK issue).
+        // QK goes one chunk group at a time, as the groups land.
         while (need_qk || need_pv) {
           bool progress = false;
           for (int pass = 0; pass < 2; ++pass) {
-            if ((pass == 0) != pv_first) {
+            if (pass == 1) {
               if (need_qk) {
                 if (!q_ok && mbar_test(smem_addr(&ctl.q_full), q_full_par)) {
                   q_ok = true;
@@ -1005,6 +1006,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (s_ok && qg < kChunkGroups &&
                     mbar_test(smem_addr(&ctl.kv_full[qstage][qg]), (kv_full_par >> qstage) & 1u)) {
+                  trace(tr, 3, 2048 + 3 * qk_issued + qg);
                   fence_proxy_async();
                   tc_fence_after();
                   issue_qk_group<nchunks>(tmem + kTmemS + 128u * qstage, sQ,
@@ -1021,7 +1023,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   need_qk = false;
                 }
               }
-            } else if (need_pv && (pv_first || !progress)) {
+            } else if (need_pv) {
               if (!p_ok && mbar_test(smem_addr(&ctl.p_full), p_full_par)) {
                 p_ok = true;
                 p_full_par ^= 1u;
@@ -1339,19 +1341,19 @@ static bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t c
   return r == CUDA_SUCCESS;
 }
 
-template <bool kBf16, int kChunks>
+template <bool kBf16, int kChunks, bool kTrace>
 static int launch_one(const FwdArgs& args, int grid, cudaStream_t stream, const CUtensorMap& tm_q,
                       const CUtensorMap& tm_ori, const CUtensorMap& tm_cmp,
                       const CUtensorMap& tm_ori16, const CUtensorMap& tm_cmp16) {
   static bool configured = false;
   if (!configured) {
-    if (cudaFuncSetAttribute(sas_fwd_kernel<kBf16, kChunks>,
+    if (cudaFuncSetAttribute(sas_fwd_kernel<kBf16, kChunks, kTrace>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemDynamic) != cudaSuccess)
       return SAS_ERR_CUDA;
     configured = true;
   }
-  sas_fwd_kernel<kBf16, kChunks><<<grid, kThreads, kSmemDynamic, stream>>>(
+  sas_fwd_kernel<kBf16, kChunks, kTrace><<<grid, kThreads, kSmemDynamic, stream>>>(
       args, tm_q, tm_ori, tm_cmp, tm_ori16, tm_cmp16);
   return cudaGetLastError() == cudaSuccess ? SAS_OK : SAS_ERR_CUDA;
 }
@@ -1378,12 +1380,16 @@ int launch_fwd(const FwdArgs& args, int grid, cudaStream_t stream) {
     tm_cmp = tm_ori;
     tm_cmp16 = tm_ori16;
   }
-  if (args.head_dim == 576)
-    return bf16 ? launch_one<true, 9>(args, grid, stream, tm_q, tm_ori, tm_cmp, tm_ori16, tm_cmp16)
-                : launch_one<false, 9>(args, grid, stream, tm_q, tm_ori, tm_cmp, tm_ori16,
-                                       tm_cmp16);
-  return bf16 ? launch_one<true, 8>(args, grid, stream, tm_q, tm_ori, tm_cmp, tm_ori16, tm_cmp16)
-              : launch_one<false, 8>(args, grid, stream, tm_q, tm_ori, tm_cmp, tm_ori16, tm_cmp16);
+  // The trace instances carry the clock-trace stores; the others have none.
+#define SAS_LAUNCH(B, C, T) launch_one<B, C, T>(args, grid, stream, tm_q, tm_ori, tm_cmp, tm_ori16, tm_cmp16)
+  const bool t = args.trace != nullptr;
+  if (args.head_dim == 576) {
+    if (bf16) return t ? SAS_LAUNCH(true, 9, true) : SAS_LAUNCH(true, 9, false);
+    return t ? SAS_LAUNCH(false, 9, true) : SAS_LAUNCH(false, 9, false);
+  }
+  if (bf16) return t ? SAS_LAUNCH(true, 8, true) : SAS_LAUNCH(true, 8, false);
+  return t ? SAS_LAUNCH(false, 8, true) : SAS_LAUNCH(false, 8, false);
+#undef SAS_LAUNCH
 }
 
 }  // namespace sas
