@@ -203,13 +203,9 @@ extern "C" int sas_fwd_execute(const SasProblem* prob, const SasFwdParams* param
   a.cmp_rows = f.cmp_kv ? f.cmp_num_blocks * a.cmp_block_size : 0;
   {
     // Key-row gather engine: TMA tile::gather4 from the four producer warps
-    // (default) or cp.async 16 B (SAS_GATHER=lsu).
-    static int gather = -1;
-    if (gather < 0) {
-      const char* e = getenv("SAS_GATHER");
-      gather = (e != nullptr && strcmp(e, "lsu") == 0) ? 0 : 1;
-    }
-    a.gather = gather;
+    // (default) or cp.async 16 B (SAS_GATHER=lsu), read at each call.
+    const char* e = getenv("SAS_GATHER");
+    a.gather = (e != nullptr && strcmp(e, "lsu") == 0) ? 0 : 1;
   }
   int rc = SAS_OK;
   if (phases & SAS_PHASE_ATTN) {

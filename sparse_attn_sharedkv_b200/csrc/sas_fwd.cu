@@ -146,6 +146,12 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
                : "memory");
 }
 
+// Raises the transaction count of the current phase without arriving.
+__device__ __forceinline__ void mbar_add_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
 // 2D tiled TMA load of one box at (x, y) into shared memory.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
                                             uint32_t bar) {
@@ -473,7 +479,7 @@ __device__ __forceinline__ SlotSrc resolve_slot(const FwdArgs& a, const Row& rv,
     } else {
       record_error(err, SAS_ERR_DEVICE, 11, pos);
     }
-  } else if (slot < rv.slots) {
+  } else if (slot < rv.window + rv.cmp) {
     const int c = slot - rv.window;
     int pos = c;
     bool ok = true;
@@ -499,6 +505,31 @@ __device__ __forceinline__ SlotSrc resolve_slot(const FwdArgs& a, const Row& rv,
   return r;
 }
 
+// Ring slot (half, row) of a ring row (kRowRing): ring index i = 64 half +
+// row holds the cache position p = i (mod 128) of [hi - 127, hi], hi being
+// the query's own position (the window's last key); it is attended when
+// p >= win_lo.  Positions below 0 have no key (zero row).
+__device__ __forceinline__ SlotSrc resolve_ring(const FwdArgs& a, const Row& rv, int half,
+                                                int row, int* err) {
+  const int hi = rv.win_lo + rv.window - 1;
+  const int i = half * 64 + row;
+  const int pos = hi - ((hi - i) & (kRingKeys - 1));
+  SlotSrc r{-1, 0, pos >= rv.win_lo};
+  if (pos >= 0) {
+    const int lb = pos / a.ori_block_size;
+    if (lb < a.ori_table_len) {
+      const int blk = __ldg(a.ori_block_table + (size_t)rv.b * a.ori_table_len + lb);
+      if (blk >= 0 && blk < a.ori_num_blocks)
+        r.row = blk * a.ori_block_size + (pos - lb * a.ori_block_size);
+      else if (blk >= a.ori_num_blocks)
+        record_error(err, SAS_ERR_DEVICE, 10, blk);
+    } else {
+      record_error(err, SAS_ERR_DEVICE, 11, pos);
+    }
+  }
+  return r;
+}
+
 // cp.async of `count` key rows of this warp's 16-key block: local key
 // lbase + k (k < count) sits at smem row key0 + lbase + k and its source is
 // (r, p) of lane lbase + k.  Rows without a source are zero-filled (src-size 0).
@@ -519,15 +550,21 @@ __device__ __forceinline__ void lsu_rows(const FwdArgs& a, uint32_t sK, int key0
   }
 }
 
-// TMA gather of this warp's 16 key rows (smem rows key0 .. key0 + 15): lanes
-// 0..3 each move a group of 4 consecutive keys with one tile::gather4 per
-// 64-column chunk (4 rows x 128 B into 512 B of the swizzled chunk).  Slots
-// without a source read an out-of-range row, which TMA fills with zeros.  A
-// group whose rows come from both caches (window / compressed boundary) is
-// moved by cp.async instead.  Lane 0 arms the chunk-group barriers with the
-// TMA bytes each of them receives.
+// Chunks of [c0, c1) that fall in chunk group cg (chunks 3 cg .. 3 cg + 2).
+__device__ __forceinline__ uint32_t group_chunks(int cg, int c0, int c1) {
+  return (uint32_t)max(0, min(3 * cg + 3, c1) - max(3 * cg, c0));
+}
+
+// TMA gather of chunks c0 .. nchunks - 1 of this warp's 16 key rows (smem
+// rows key0 .. key0 + 15): lanes 0..3 each move a group of 4 consecutive
+// keys with one tile::gather4 per 64-column chunk (4 rows x 128 B into 512 B
+// of the swizzled chunk).  Slots without a source read an out-of-range row,
+// which TMA fills with zeros.  A group whose rows come from both caches
+// (window / compressed boundary) is moved by cp.async instead (whole rows).
+// Lane 0 arms the chunk-group barriers with the TMA bytes each receives.
 __device__ __forceinline__ void tma_rows(const FwdArgs& a, const CUtensorMap* tm_ori,
-                                         const CUtensorMap* tm_cmp, int nchunks, uint32_t sK,
+                                         const CUtensorMap* tm_cmp, int c0, int nchunks,
+                                         uint32_t sK,
                                          const uint32_t (&bar)[kChunkGroups], int key0, int r,
                                          int p, int lane, uint32_t row_bytes, int gran) {
   const int g = lane & 3;
@@ -551,7 +588,7 @@ __device__ __forceinline__ void tma_rows(const FwdArgs& a, const CUtensorMap* tm
     const uint32_t groups = (uint32_t)(4 - __popc(mixed_mask));
 #pragma unroll
     for (int cg = 0; cg < kChunkGroups; ++cg)
-      mbar_expect_tx(bar[cg], groups * 4u * 128u * (uint32_t)min(3, nchunks - 3 * cg));
+      mbar_expect_tx(bar[cg], groups * 4u * 128u * group_chunks(cg, c0, nchunks));
   }
   __syncwarp();
   if (lane < 4 && !mixed) {
@@ -561,12 +598,55 @@ __device__ __forceinline__ void tma_rows(const FwdArgs& a, const CUtensorMap* tm
     for (int i = 0; i < 4; ++i)
       if (pool[i] < 0 || row[i] < 0) row[i] = sentinel;
     const uint32_t dst = sK + (uint32_t)(key0 + 4 * lane) * 128u;
-    for (int c = 0; c < nchunks; ++c)
+    for (int c = c0; c < nchunks; ++c)
       tma_gather4(dst + c * kChunkBytes, m, c * 64, row[0], row[1], row[2], row[3],
                   bar[chunk_group(c)]);
   }
   for (uint32_t mm = mixed_mask; mm != 0u; mm &= mm - 1u)
     lsu_rows(a, sK, key0, 4 * (__ffs(mm) - 1), 4, r, p, lane, row_bytes, gran);
+}
+
+// This warp's 16 key rows of a tile (smem rows 16 pw .. 16 pw + 15) into the
+// stage at sK, chunks c0 .. nchunks - 1: one 16-row TMA box per chunk when
+// the rows are 16 consecutive rows of one cache (window keys inside one
+// page, contiguous compressed positions), else tile::gather4 groups
+// (tma_rows); cp.async of whole rows in LSU mode (c0 = 0).  Lane 0 arrives
+// once on each chunk-group barrier, arming the TMA bytes.
+__device__ __forceinline__ void load_tile_rows(const FwdArgs& a, const SlotSrc& sa, int c0,
+                                               int nchunks, uint32_t sK,
+                                               const uint32_t (&bar)[kChunkGroups], int pw,
+                                               int lane, bool lsu, uint32_t row_bytes, int gran,
+                                               const CUtensorMap* tm_ori,
+                                               const CUtensorMap* tm_cmp,
+                                               const CUtensorMap* tm_ori16,
+                                               const CUtensorMap* tm_cmp16) {
+  if (lsu) {
+    __syncwarp();
+    if (lane == 0) {
+#pragma unroll
+      for (int cg = 0; cg < kChunkGroups; ++cg) mbar_arrive(bar[cg]);
+    }
+    lsu_rows(a, sK, pw * 16, 0, 16, sa.row, sa.pool, lane, row_bytes, gran);
+    return;
+  }
+  const int row0 = __shfl_sync(0xffffffffu, sa.row, 0);
+  const int pool0 = __shfl_sync(0xffffffffu, sa.pool, 0);
+  const bool run16 = __all_sync(0xffffffffu, pool0 >= 0 && sa.pool == pool0 && sa.row >= 0 &&
+                                                 sa.row == row0 + (lane & 15));
+  if (run16) {
+    if (lane == 0) {
+#pragma unroll
+      for (int cg = 0; cg < kChunkGroups; ++cg)
+        mbar_expect_tx(bar[cg], 16u * 128u * group_chunks(cg, c0, nchunks));
+      const CUtensorMap* m = (pool0 == 1) ? tm_cmp16 : tm_ori16;
+      const uint32_t dst = sK + (uint32_t)(pw * 16) * 128u;
+      for (int c = c0; c < nchunks; ++c)
+        tma_load_2d(dst + c * kChunkBytes, m, c * 64, row0, bar[chunk_group(c)]);
+    }
+  } else {
+    tma_rows(a, tm_ori, tm_cmp, c0, nchunks, sK, bar, pw * 16, sa.row, sa.pool, lane, row_bytes,
+             gran);
+  }
 }
 
 // Coalesced store of one warp's 32 rows x 32 bytes: lane i holds row i's
@@ -802,6 +882,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t kv_empty_par = 3u;  // bit = stage
     int stage = 0, produced = 0;
     bool ok = true;
+    // Ring state: the stages hold the ring of sequence ring_b around
+    // position ring_hi, ring half h in stage h ^ ring_sigma.
+    bool ring_live = false;
+    int ring_b = -1, ring_hi = 0, ring_sigma = 0;
     RowStream rs(rows, span.r0, span.r1);
     for (int r = span.r0; ok && span.r0 >= 0 && r <= span.r1; ++r) {
       const Row rv = rs.take(r);
@@ -809,6 +893,75 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int ja = (r == span.r0) ? span.t0 : 0;
       const int jb = (r == span.r1) ? span.t1 : (tiles > 0 ? tiles : 1);
       if (tiles == 0 || ja >= jb) continue;
+
+      // ---- ring rows: the window stays in the stages from query to query ----
+      // The next query of the sequence (position hi + 1) keeps every key but
+      // the one at hi - 127, whose slot receives the new key: per stage, the
+      // rope chunk (overwritten by P) is loaded again for all 64 rows and,
+      // in the stage holding the new key, chunks 0..7 of its 4-row group.
+      // Any other row (a piece of a split row, another sequence, a gap)
+      // loads both stages whole.
+      if ((rv.flags & kRowRing) && !lsu && ja == 0 && jb == 2) {
+        const int hi = rv.win_lo + rv.window - 1;
+        const bool warm = ring_live && rv.b == ring_b && hi == ring_hi + 1;
+        if (!warm) ring_sigma = stage;
+        const int new_half = (hi >> 6) & 1, new_row = hi & 63;
+        const int c_new = min(nchunks, kPChunk);  // chunks of the new row not in the rope load
+        for (int k = 0; k < 2; ++k) {
+          const int half = stage ^ ring_sigma;
+          const SlotSrc sa = resolve_ring(args, rv, half, pw * 16 + (lane & 15), err);
+          const uint32_t va_cur = __ballot_sync(0xffffffffu, sa.valid);
+          if (leader && lane == 0) trace(tr, 0, 3 * produced);
+          if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.kv_empty[stage],
+                                                (kv_empty_par >> stage) & 1u, err, 2))) {
+            ok = false;
+            break;
+          }
+          if (leader && lane == 0) trace(tr, 0, 3 * produced + 1);
+          kv_empty_par ^= 1u << stage;
+          uint32_t bar[kChunkGroups];
+#pragma unroll
+          for (int cg = 0; cg < kChunkGroups; ++cg) bar[cg] = smem_addr(&ctl.kv_full[stage][cg]);
+          const uint32_t sK = sK0 + stage * kStageBytes;
+          if (lane == 0) ctl.valid[stage][pw] = (uint16_t)(va_cur & 0xffffu);
+          const bool owner = warm && half == new_half && (new_row >> 4) == pw;
+          if (owner && lane == 0) {
+#pragma unroll
+            for (int cg = 0; cg < kChunkGroups; ++cg)
+              mbar_add_tx(bar[cg], 4u * 128u * group_chunks(cg, 0, c_new));
+          }
+          __syncwarp();
+          load_tile_rows(args, sa, warm ? kPChunk : 0, nchunks, sK, bar, pw, lane, false,
+                         row_bytes, gran, &tm_ori, &tm_cmp, &tm_ori16, &tm_cmp16);
+          if (owner) {
+            // chunks 0 .. c_new - 1 of the 4-row group holding the new key
+            // (its three neighbours are rewritten with the same rows)
+            const int g = (new_row & 15) >> 2;
+            int rr[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              rr[q] = __shfl_sync(0xffffffffu, sa.row, 4 * g + q);
+              if (rr[q] < 0) rr[q] = args.ori_rows;  // out of range: zero-filled
+            }
+            if (lane == 0) {
+              const uint32_t dst = sK + (uint32_t)(pw * 16 + 4 * g) * 128u;
+              for (int c = 0; c < c_new; ++c)
+                tma_gather4(dst + c * kChunkBytes, &tm_ori, c * 64, rr[0], rr[1], rr[2], rr[3],
+                            bar[chunk_group(c)]);
+            }
+          }
+#pragma unroll
+          for (int cg = 0; cg < kChunkGroups; ++cg) cp_async_arrive_noinc(bar[cg]);
+          if (leader && lane == 0) trace(tr, 0, 3 * produced + 2);
+          ++produced;
+          stage ^= 1;
+        }
+        ring_live = ok;
+        ring_b = rv.b;
+        ring_hi = hi;
+        continue;
+      }
+      ring_live = false;
 
       // ---- key tiles (key bounds precomputed by the planner) ----
       QueryKeys qk;
@@ -854,38 +1007,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int cg = 0; cg < kChunkGroups; ++cg) bar[cg] = smem_addr(&ctl.kv_full[stage][cg]);
         const uint32_t sK = sK0 + stage * kStageBytes;
         if (lane == 0) ctl.valid[stage][pw] = (uint16_t)(va_cur & 0xffffu);
-        if (lsu) {
-          __syncwarp();
-          if (lane == 0) {
-#pragma unroll
-            for (int cg = 0; cg < kChunkGroups; ++cg) mbar_arrive(bar[cg]);
-          }
-          lsu_rows(args, sK, pw * 16, 0, 16, sa.row, sa.pool, lane, row_bytes, gran);
-        } else {
-          // The warp's 16 slots read 16 consecutive rows of one cache (window
-          // keys inside one page, contiguous compressed positions): one
-          // 16-row TMA box per chunk instead of four gather4 ops.
-          const int row0 = __shfl_sync(0xffffffffu, sa.row, 0);
-          const int pool0 = __shfl_sync(0xffffffffu, sa.pool, 0);
-          const bool run16 = __all_sync(0xffffffffu, pool0 >= 0 && sa.pool == pool0 &&
-                                                         sa.row >= 0 &&
-                                                         sa.row == row0 + (lane & 15));
-          if (run16) {
-            if (lane == 0) {
-#pragma unroll
-              for (int cg = 0; cg < kChunkGroups; ++cg)
-                mbar_expect_tx(bar[cg], 16u * 128u * (uint32_t)min(3, nchunks - 3 * cg));
-              const CUtensorMap* m = (pool0 == 1) ? &tm_cmp16 : &tm_ori16;
-              const uint32_t dst = sK + (uint32_t)(pw * 16) * 128u;
-#pragma unroll
-              for (int c = 0; c < nchunks; ++c)
-                tma_load_2d(dst + c * kChunkBytes, m, c * 64, row0, bar[chunk_group(c)]);
-            }
-          } else {
-            tma_rows(args, &tm_ori, &tm_cmp, nchunks, sK, bar, pw * 16, sa.row, sa.pool, lane,
-                     row_bytes, gran);
-          }
-        }
+        load_tile_rows(args, sa, 0, nchunks, sK, bar, pw, lane, lsu, row_bytes, gran, &tm_ori,
+                       &tm_cmp, &tm_ori16, &tm_cmp16);
 #pragma unroll
         for (int cg = 0; cg < kChunkGroups; ++cg) cp_async_arrive_noinc(bar[cg]);
         if (leader && lane == 0) trace(tr, 0, 3 * produced + 2);

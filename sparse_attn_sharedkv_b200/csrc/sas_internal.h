@@ -33,7 +33,7 @@ enum RowField {
   R_BATCH,         // b
   R_POS,           // s: query index inside the batch
   R_SLOTS,         // key slots: window + compressed (before masking)
-  R_FLAGS,         // bit0: padded BSND slot (write zeros)
+  R_FLAGS,         // bit0: padded BSND slot (write zeros); bit1: ring row
   R_FIRST_WORKER,  // first worker that processes a tile of this row (diagnostic)
   R_PARTIAL_BASE,  // partial slot of piece 0, or -1 when the row is not split
   R_WINDOW,        // window slots W (slots [0, W) are window keys)
@@ -43,6 +43,12 @@ enum RowField {
   R_PAD            // unused
 };
 constexpr int kRowPadded = 1;
+// bit1: ring row.  A pure sliding window of at most kRingKeys keys is kept
+// in the two K stages as a ring over cache positions (position p at stage
+// half (p >> 6) & 1, row p & 63), so that the next query of the sequence
+// reuses every key but one.  Ring rows always span two 64-key tiles.
+constexpr int kRowRing = 2;
+constexpr int32_t kRingKeys = 128;
 constexpr int32_t kPlanMagic = 0x53415331;  // "SAS1"
 
 inline int64_t align64(int64_t x) { return (x + 63) / 64 * 64; }
@@ -91,6 +97,22 @@ SAS_HD inline QueryKeys query_keys(int32_t scenario, int32_t act_q, int32_t act_
     k.cmp = c;
   }
   return k;
+}
+
+// Windows of 65..128 keys with no compressed branch run as ring rows.
+SAS_HD inline bool ring_window(int32_t scenario, int32_t win_left) {
+  return scenario == SAS_SCENARIO_SWA && win_left >= 64 && win_left < kRingKeys;
+}
+
+// Key slots of a query row and its flags (both planners).
+SAS_HD inline int32_t row_slots(const QueryKeys& k, int32_t scenario, int32_t win_left,
+                                int32_t* flags) {
+  if (ring_window(scenario, win_left) && k.window > 0) {
+    *flags = kRowRing;
+    return kRingKeys;
+  }
+  *flags = 0;
+  return k.window + k.cmp;
 }
 
 }  // namespace sas

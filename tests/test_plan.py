@@ -47,6 +47,7 @@ def build_plan(p, sms):
 
 
 ROW_INTS = 12  # token, b, s, slots, flags, first_worker, partial_base, window, win_lo, cmp, thr, pad
+RING = 2  # flags bit: pure sliding window kept as a 128-position ring (two tiles)
 
 
 def rows_of(plan):
@@ -148,6 +149,17 @@ def kernel_slot_positions(case, plan):
             lim = min(ja * 64 - Wn, ncmp)
             stopped = any(idx[t, c] == -1 for c in range(max(lim, 0)))
         got = out.setdefault(r, [])
+        if flags & RING:
+            assert scen == 1 and slots == 128 and 64 <= case.ori_win_left < 128 and Wn > 0
+            if (ja, jb) == (0, 2):
+                # ring slot (half, row) holds position p = 64 half + row (mod 128)
+                # of [hi - 127, hi]; attended when p >= lo
+                hi = row_lo + Wn - 1
+                for i in range(128):
+                    p = hi - ((hi - i) % 128)
+                    if p >= row_lo:
+                        got.append(("ori", p))
+                continue
         for j in range(ja, jb):
             m1 = 0
             if scen == 3:
@@ -159,7 +171,7 @@ def kernel_slot_positions(case, plan):
                 slot = j * 64 + key
                 if slot < Wn:
                     got.append(("ori", lo + slot))
-                elif slot < slots:
+                elif slot < Wn + row_cmp:
                     c = slot - Wn
                     if scen == 3:
                         pos = int(idx[t, c])
@@ -181,6 +193,10 @@ SLOT_CASES = [
          kv_lens=(1300, 1500)),
     dict(seed=4, layout_q="TND", scenario=2, ratio=8, q_lens=(6, 2), kv_lens=(1400, 600)),
     dict(seed=5, layout_q="TND", scenario=1, q_lens=(70, 3), kv_lens=(100, 3)),
+    dict(seed=7, layout_q="TND", scenario=1, q_lens=(300, 2, 64), kv_lens=(1000, 130, 64)),
+    dict(seed=8, layout_q="BSND", B=2, scenario=1, win_left=100, q_lens=(5, 9),
+         kv_lens=(700, 9)),
+    dict(seed=9, layout_q="TND", scenario=1, win_left=300, q_lens=(40, 3), kv_lens=(900, 50)),
     dict(seed=6, layout_q="TND", scenario=3, ratio=1, win_left=-1, K=256, idx_mode="dirty",
          q_lens=(4, 4), kv_lens=(600, 300)),
 ]
@@ -220,7 +236,10 @@ def test_kernel_slot_logic_matches_oracle(kw, sms):
             exp += [("cmp", x) for x in O.scfa_positions(idx[t], akv, aq, s, case.cmp_ratio)]
         elif scen == 2:
             exp += [("cmp", x) for x in range(max(O.cmp_threshold(akv, aq, s, case.cmp_ratio), 0))]
-        assert got.get(r, []) == exp, (r, t)
+        if row[4] & RING:
+            assert sorted(got.get(r, [])) == sorted(exp), (r, t)
+        else:
+            assert got.get(r, []) == exp, (r, t)
 
 
 def test_plan_rejects_bad_problems():
