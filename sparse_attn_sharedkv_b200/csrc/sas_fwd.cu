@@ -307,12 +307,11 @@ __device__ __forceinline__ uint32_t swz(int row, int granule) {
 
 struct Ctl {
   uint64_t kv_full[2][kChunkGroups];  // [stage][chunk group]
-  uint64_t kv_empty[2];
+  uint64_t kv_empty[2];  // PV number k (stage k % 2) completes phase k / 2 of kv_empty[k % 2]
   uint64_t q_full, q_empty;
   uint64_t s_full[2];
   uint64_t s_empty[2];
   uint64_t p_full, o_free, drain;
-  uint64_t pv_done[2];            // PV number k completes phase k/2 of pv_done[k % 2]
   uint64_t xbar[2];               // softmax partner exchange (bounded, no bar.sync)
   uint32_t tmem_base;
   volatile int abort;
@@ -359,8 +358,10 @@ struct RowStream {
 // Diagnostic clock trace of one CTA (FwdArgs::trace_cta), compiled only into
 // the kernel instances launched with a trace buffer: 4 regions of 8192
 // entries: producer, MMA and softmax events per tile; in region 3 the
-// epilogue per row (from 0), the chunk-group landings seen by the MMA issuer
-// (from 2048), Q load issues (from 4096) and Q arrivals (from 6144).
+// epilogue per row (from 0), MMA loop iterations (from 1024), the
+// chunk-group landings seen by the MMA issuer (from 2048), Q load issues
+// (from 4096) and Q arrivals (from 6144); in region 0 from 4096 the S
+// releases of the four softmax warps per tile.
 constexpr int kTraceRegion = 8192;
 __device__ __forceinline__ void trace(long long* tr, int region, int idx) {
   if (tr != nullptr && idx >= 0 && idx < kTraceRegion)
@@ -844,8 +845,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(smem_addr(&ctl.q_full), 1);
     mbar_init(smem_addr(&ctl.q_empty), 1);
     mbar_init(smem_addr(&ctl.p_full), kSoftmaxThreads);
-    mbar_init(smem_addr(&ctl.pv_done[0]), 1);
-    mbar_init(smem_addr(&ctl.pv_done[1]), 1);
     mbar_init(smem_addr(&ctl.o_free), kEpiThreads);
     mbar_init(smem_addr(&ctl.o_full), 1);
     mbar_init(smem_addr(&ctl.drain), 1);
@@ -1067,126 +1066,108 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t q_full_par = 0u, p_full_par = 0u, o_free_par = 1u;
       int pv_issued = 0, qk_issued = 0, q_seen = 0;
       bool ok = true;
-      // The worker's tiles form one stream across rows: QK(t+1) may open the
-      // next row (it then waits for that row's Q) while PV(t) is pending, so
-      // a row boundary does not drain the pipe.  Tile t uses K stage t % 2
-      // and S buffer t % 2.
+      // The worker's tiles form one stream across rows; tile t uses K stage
+      // t % 2 and S buffer t % 2.  QKs and PVs are issued as two independent
+      // in-order streams, each step as soon as its inputs are in: PV(t)
+      // after QK(t) and P(t) (and, for a row's first PV, the epilogue's
+      // release of O); QK(t) one chunk group at a time after its Q, its S
+      // buffer (released by softmax(t - 2)) and the group's K rows.  A PV
+      // that is ready goes first: it releases the K stage that the load two
+      // tiles ahead waits for.  Nothing else orders the two streams, so a row
+      // boundary or a late softmax does not hold back the next QK.
       TileCursor qc(rows, span), pc(rows, span);
       int qstage = 0, pstage = 0;
-      // QK of the first tile, blocking.
-      if (qc.valid) {
-        if (!wait_bar(&ctl, &ctl.q_full, q_full_par, err, 22)) ok = false;
-        q_full_par ^= 1u;
-        trace(tr, 3, 6144 + q_seen++);
-        trace(tr, 1, 4 * qk_issued);
-        for (int cg = 0; cg < kChunkGroups && ok; ++cg) {
-          if (!wait_bar(&ctl, &ctl.kv_full[0][cg], 0u, err, 20)) {
+      int pending = 0;            // tiles whose QK is issued and PV is not
+      int qg = 0;                 // chunk groups of QK(qc) issued
+      bool q_ok = false, s_ok = false, p_ok = false, o_ok = false;
+      long long t_idle = clock64();
+      while (ok && (qc.valid || pending > 0)) {
+        bool progress = false;
+        // ---- PV of the oldest tile whose QK is issued ----
+        if (pending > 0) {
+          if (!p_ok && mbar_test(smem_addr(&ctl.p_full), p_full_par)) {
+            p_ok = true;
+            p_full_par ^= 1u;
+          }
+          if (!o_ok) {
+            if (!pc.first()) {
+              o_ok = true;
+            } else if (mbar_test(smem_addr(&ctl.o_free), o_free_par)) {
+              o_ok = true;
+              o_free_par ^= 1u;
+            }
+          }
+          if (p_ok && o_ok) {
+            trace(tr, 1, 4 * pv_issued + 2);
+            fence_proxy_async();
+            tc_fence_after();
+            issue_pv(tmem + kTmemO, sK0 + pstage * kStageBytes, idesc_pv, pc.first());
+            trace(tr, 1, 4 * pv_issued + 3);
+            tc_commit(smem_addr(&ctl.kv_empty[pstage]));
+            if (pc.last()) tc_commit(smem_addr(&ctl.o_full));
+            ++pv_issued;
+            --pending;
+            pc.advance();
+            pstage ^= 1;
+            p_ok = o_ok = false;
+            progress = true;
+          }
+        }
+        // ---- QK of the next tile, one chunk group at a time ----
+        if (qc.valid) {
+          if (!q_ok) {
+            if (!qc.first()) {
+              q_ok = true;
+            } else if (mbar_test(smem_addr(&ctl.q_full), q_full_par)) {
+              q_ok = true;
+              q_full_par ^= 1u;
+              trace(tr, 3, 6144 + q_seen++);
+            }
+          }
+          if (q_ok && !s_ok) trace(tr, 3, 1025 + 2 * qk_issued);
+          if (q_ok && !s_ok &&
+              mbar_test(smem_addr(&ctl.s_empty[qstage]), (s_empty_par >> qstage) & 1u)) {
+            s_ok = true;
+            s_empty_par ^= 1u << qstage;
+            trace(tr, 1, 4 * qk_issued);
+          }
+          if (s_ok &&
+              mbar_test(smem_addr(&ctl.kv_full[qstage][qg]), (kv_full_par >> qstage) & 1u)) {
+            trace(tr, 3, 2048 + 3 * qk_issued + qg);
+            fence_proxy_async();
+            tc_fence_after();
+            issue_qk_group<nchunks>(tmem + kTmemS + 128u * qstage, sQ,
+                                    sK0 + qstage * kStageBytes, idesc_qk, qg);
+            progress = true;
+            if (++qg == kChunkGroups) {
+              kv_full_par ^= 1u << qstage;
+              trace(tr, 1, 4 * qk_issued + 1);
+              ++qk_issued;
+              tc_commit(smem_addr(&ctl.s_full[qstage]));
+              if (qc.last()) tc_commit(smem_addr(&ctl.q_empty));
+              trace(tr, 3, 1024 + 2 * qk_issued);
+              qc.advance();
+              qstage ^= 1;
+              ++pending;
+              qg = 0;
+              q_ok = s_ok = false;
+            }
+          }
+        }
+        if (progress) {
+          t_idle = clock64();
+        } else {
+          if (ctl.abort) {
             ok = false;
             break;
           }
-          fence_proxy_async();
-          tc_fence_after();
-          issue_qk_group<nchunks>(tmem + kTmemS, sQ, sK0, idesc_qk, cg);
-        }
-        if (ok) {
-          kv_full_par ^= 1u;
-          s_empty_par ^= 1u;  // buffer 0 was free
-          trace(tr, 1, 4 * qk_issued + 1);
-          ++qk_issued;
-          tc_commit(smem_addr(&ctl.s_full[0]));
-          if (qc.last()) tc_commit(smem_addr(&ctl.q_empty));
-          qc.advance();
-          qstage = 1;
-        }
-      }
-      while (ok && pc.valid) {
-        // Pending: PV of tile pc (stage pstage) and QK of tile qc (stage
-        // qstage, S buffer qstage), if any.
-        bool need_qk = qc.valid, need_pv = true;
-        bool q_ok = !qc.valid || !qc.first(), s_ok = false;
-        int qg = 0;  // chunk groups of the QK issued
-        bool p_ok = false, o_ok = !pc.first();
-        long long t0 = clock64();
-        // PV goes first whenever its P is in: it releases the K stage that
-        // the load two tiles ahead waits for, which is the longer chain
-        // (issuing the next QK first delayed the stage by the whole QK issue).
-        // QK goes one chunk group at a time, as the groups land.
-        while (need_qk || need_pv) {
-          bool progress = false;
-          for (int pass = 0; pass < 2; ++pass) {
-            if (pass == 1) {
-              if (need_qk) {
-                if (!q_ok && mbar_test(smem_addr(&ctl.q_full), q_full_par)) {
-                  q_ok = true;
-                  q_full_par ^= 1u;
-                  trace(tr, 3, 6144 + q_seen++);
-                }
-                if (q_ok && !s_ok &&
-                    mbar_test(smem_addr(&ctl.s_empty[qstage]), (s_empty_par >> qstage) & 1u)) {
-                  s_ok = true;
-                  s_empty_par ^= 1u << qstage;
-                  trace(tr, 1, 4 * qk_issued);
-                }
-                if (s_ok && qg < kChunkGroups &&
-                    mbar_test(smem_addr(&ctl.kv_full[qstage][qg]), (kv_full_par >> qstage) & 1u)) {
-                  trace(tr, 3, 2048 + 3 * qk_issued + qg);
-                  fence_proxy_async();
-                  tc_fence_after();
-                  issue_qk_group<nchunks>(tmem + kTmemS + 128u * qstage, sQ,
-                                          sK0 + qstage * kStageBytes, idesc_qk, qg);
-                  ++qg;
-                  progress = true;
-                }
-                if (qg == kChunkGroups) {
-                  kv_full_par ^= 1u << qstage;
-                  trace(tr, 1, 4 * qk_issued + 1);
-                  ++qk_issued;
-                  tc_commit(smem_addr(&ctl.s_full[qstage]));
-                  if (qc.last()) tc_commit(smem_addr(&ctl.q_empty));
-                  need_qk = false;
-                }
-              }
-            } else if (need_pv) {
-              if (!p_ok && mbar_test(smem_addr(&ctl.p_full), p_full_par)) {
-                p_ok = true;
-                p_full_par ^= 1u;
-              }
-              if (!o_ok && mbar_test(smem_addr(&ctl.o_free), o_free_par)) {
-                o_ok = true;
-                o_free_par ^= 1u;
-              }
-              if (p_ok && o_ok) {
-                trace(tr, 1, 4 * pv_issued + 2);
-                fence_proxy_async();
-                tc_fence_after();
-                issue_pv(tmem + kTmemO, sK0 + pstage * kStageBytes, idesc_pv, pc.first());
-                trace(tr, 1, 4 * pv_issued + 3);
-                tc_commit(smem_addr(&ctl.kv_empty[pstage]));
-                tc_commit(smem_addr(&ctl.pv_done[pv_issued & 1]));
-                if (pc.last()) tc_commit(smem_addr(&ctl.o_full));
-                ++pv_issued;
-                need_pv = false;
-                progress = true;
-              }
-            }
-          }
-          if (!progress) {
-            if (ctl.abort) { ok = false; break; }
-            if (clock64() - t0 > kWaitCycles) {
-              record_error(err, SAS_ERR_DEVICE, 23, pv_issued);
-              ctl.abort = 1;
-              ok = false;
-              break;
-            }
+          if (clock64() - t_idle > kWaitCycles) {
+            record_error(err, SAS_ERR_DEVICE, 23, pv_issued);
+            ctl.abort = 1;
+            ok = false;
+            break;
           }
         }
-        if (!ok) break;
-        if (qc.valid) {
-          qc.advance();
-          qstage ^= 1;
-        }
-        pc.advance();
-        pstage ^= 1;
       }
       // Drain: the commit arrives once every MMA issued above has finished,
       // so TMEM is never released under an in-flight MMA (also on abort).
@@ -1267,14 +1248,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t kv_full_par = 0u, s_full_par = 0u;  // bit = stage / S buffer
     int pv_count = 0;  // PVs released by this thread's p_full arrivals so far
     int rows_done = 0;
-    // Completion of PV number k: phase k/2 of pv_done[k % 2].  When softmax
-    // waits for PV k, PV k-2 is complete (the S of the current tile is only
-    // produced after the PV two tiles back freed its K stage) and PV k+2 is
-    // not yet released, so pv_done[k % 2] is exactly one phase short of or
-    // at the awaited completion and the parity test is exact, although most
-    // completions are never waited for.
+    // Completion of PV number k: phase k/2 of kv_empty[k % 2] (its commit
+    // also releases the K stage).  When softmax waits for PV k, PV k-2 is
+    // complete (the S of the current tile is only produced after the PV two
+    // tiles back freed its K stage) and PV k+2 is not yet released, so
+    // kv_empty[k % 2] is exactly one phase short of or at the awaited
+    // completion and the parity test is exact.
     auto wait_pv = [&](int k, int site) -> bool {
-      return wait_bar(&ctl, &ctl.pv_done[k & 1], (uint32_t)((k >> 1) & 1), err, site);
+      return wait_bar(&ctl, &ctl.kv_empty[k & 1], (uint32_t)((k >> 1) & 1), err, site);
     };
     uint32_t xph = 0u;  // bit = exchange barrier
     int stage = 0, sbuf = 0, xpar = 0;
@@ -1343,6 +1324,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_before();
         mbar_arrive(smem_addr(&ctl.s_empty[sb]));
+        if (lane == 0) trace(tr, 0, 4096 + 4 * pv_count + warp);
         const uint32_t vb = (uint32_t)ctl.valid[st][2 * half] |
                             ((uint32_t)ctl.valid[st][2 * half + 1] << 16);
         float x[32];
