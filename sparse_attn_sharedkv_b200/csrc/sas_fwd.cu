@@ -368,6 +368,12 @@ __device__ __forceinline__ void trace(long long* tr, int region, int idx) {
     tr[region * kTraceRegion + idx] = clock64();
 }
 
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
 __device__ void record_error(int* err, int code, int site, int detail) {
   if (err != nullptr && atomicCAS(err, 0, code) == 0) {
     err[1] = site;
@@ -823,6 +829,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int nchunks = kChunks;  // d_qk / 64
   int* err = args.err;
   long long* tr = (kTrace && (int)blockIdx.x == args.trace_cta) ? args.trace : nullptr;
+  // Trace instances also record every CTA's start and end on the global
+  // timer (ns), region 2 from 6144: [2 CTA] start, [2 CTA + 1] end.
+  if (kTrace && threadIdx.x == 0 && args.trace != nullptr && blockIdx.x < 1024u)
+    args.trace[2 * kTraceRegion + 6144 + 2 * blockIdx.x] = (long long)global_ns();
 
   // 1024-byte aligned tile area.
   const uint32_t raw = smem_addr(smem_raw);
@@ -972,13 +982,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int* idx_row = (args.scenario == SAS_SCENARIO_SCFA)
                                ? args.cmp_indices + (size_t)rv.token * args.topk
                                : nullptr;
-      // Slots before this piece may hold a -1 that stops the scan.
+      // Slots before this piece may hold a -1 that stops the scan: 512
+      // indices per step, 16 independent loads per lane in flight.
       bool stopped = false;
       if (idx_row != nullptr && ja > 0) {
         const int lim = min(ja * kTileKeys - rv.window, qk.cmp);
-        for (int c0 = 0; c0 < lim && !stopped; c0 += 32) {
-          const int c = c0 + lane;
-          const bool m1 = (c < lim) && (__ldg(idx_row + c) == -1);
+        for (int c0 = 0; c0 < lim && !stopped; c0 += 512) {
+          bool m1 = false;
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            const int c = c0 + 32 * u + lane;
+            m1 |= (c < lim) && (__ldg(idx_row + c) == -1);
+          }
           stopped = __any_sync(0xffffffffu, m1);
         }
       }
@@ -1405,6 +1420,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (kTrace && threadIdx.x == 0 && args.trace != nullptr && blockIdx.x < 1024u)
+    args.trace[2 * kTraceRegion + 6144 + 2 * blockIdx.x + 1] = (long long)global_ns();
   if (warp == kMmaWarp) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
