@@ -61,6 +61,12 @@ constexpr int kProducerWarp0 = 4;  // producer warps 4..7 gather key rows
 constexpr int kNumProducerWarps = 4;
 constexpr int kMmaWarp = 8;
 constexpr int kQWarp = 9;          // loads Q tiles by TMA, prefetches the next row's Q into L2
+// Warps 10 and 11 issue the TMA loads of chunks kHelperChunk0.. (chunk group
+// 2) of the rows that producer warps 2h, 2h + 1 resolved, so that a gathered
+// tile's ~144 TMA ops spread over six issuing warps instead of four.
+constexpr int kHelperWarp0 = 10;
+constexpr int kNumHelperWarps = 2;
+constexpr int kHelperChunk0 = 6;
 constexpr int kEpiWarp0 = 12;      // epilogue warps 12..15 (TMEM lane quarters 0..3)
 constexpr int kNumEpiWarps = 4;
 constexpr int kThreads = 32 * 16;  // warps 10, 11 have no role
@@ -313,6 +319,9 @@ struct Ctl {
   uint64_t s_empty[2];
   uint64_t p_full, o_free, drain;
   uint64_t xbar[2];               // softmax partner exchange (bounded, no bar.sync)
+  uint64_t gready[kNumHelperWarps][2];  // [helper][stage]: the tile's sources are in gsrc
+  int32_t gsrc_row[2][kTileKeys];       // [stage][slot]: source row of each key slot
+  int8_t gsrc_pool[2][kTileKeys];       // [stage][slot]: source cache (-1: none)
   uint32_t tmem_base;
   volatile int abort;
   uint16_t valid[2][4];          // per stage: slot bits of keys 16w..16w+15
@@ -656,6 +665,67 @@ __device__ __forceinline__ void load_tile_rows(const FwdArgs& a, const SlotSrc& 
   }
 }
 
+// Gather helper h: chunks kHelperChunk0 .. nchunks - 1 of tile rows 32 h ..
+// 32 h + 31 (lane l: row 32 h + l), whose sources producer warps 2h and
+// 2h + 1 left in gsrc.  Per 16-row block the same split as the producer's:
+// a 16-row box per chunk when the block is 16 consecutive rows of one cache,
+// else tile::gather4 per 4-row group; a group that mixes the two caches was
+// moved whole by the producer's cp.async.  Lane 0 arrives once on the chunk
+// group 2 barrier, arming the bytes of all ops.
+__device__ __forceinline__ void helper_rows(const FwdArgs& a, const CUtensorMap* tm_ori,
+                                            const CUtensorMap* tm_cmp,
+                                            const CUtensorMap* tm_ori16,
+                                            const CUtensorMap* tm_cmp16, const int32_t* gr,
+                                            const int8_t* gp, int h, int lane, uint32_t sK,
+                                            uint32_t bar, int nchunks) {
+  const int row = gr[32 * h + lane];
+  const int pool = gp[32 * h + lane];
+  const uint32_t nch = (uint32_t)(nchunks - kHelperChunk0);
+  const int row0 = __shfl_sync(0xffffffffu, row, lane & 16);
+  const int pool0 = __shfl_sync(0xffffffffu, pool, lane & 16);
+  const uint32_t run = __ballot_sync(0xffffffffu, pool0 >= 0 && pool == pool0 && row >= 0 &&
+                                                      row == row0 + (lane & 15));
+  const bool run_blk = ((run >> (lane & 16)) & 0xffffu) == 0xffffu;
+  const int gl = lane & ~3;
+  int prow[4], ppool[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    prow[i] = __shfl_sync(0xffffffffu, row, gl + i);
+    ppool[i] = __shfl_sync(0xffffffffu, pool, gl + i);
+  }
+  int P = -1;
+  bool mixed = false;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (ppool[i] >= 0) {
+      if (P < 0) P = ppool[i];
+      else if (ppool[i] != P) mixed = true;
+    }
+  }
+  const bool box_leader = run_blk && (lane & 15) == 0;
+  const bool grp_leader = !run_blk && (lane & 3) == 0 && !mixed;
+  const uint32_t nbox = (uint32_t)__popc(__ballot_sync(0xffffffffu, box_leader));
+  const uint32_t ngrp = (uint32_t)__popc(__ballot_sync(0xffffffffu, grp_leader));
+  if (lane == 0) mbar_expect_tx(bar, (nbox * 16u + ngrp * 4u) * 128u * nch);
+  __syncwarp();
+  if (box_leader) {
+    const CUtensorMap* m = (pool0 == 1) ? tm_cmp16 : tm_ori16;
+    const uint32_t dst = sK + (uint32_t)(32 * h + (lane & 16)) * 128u;
+    for (int c = kHelperChunk0; c < nchunks; ++c)
+      tma_load_2d(dst + c * kChunkBytes, m, c * 64, row0, bar);
+  }
+  if (grp_leader) {
+    const CUtensorMap* m = (P == 1) ? tm_cmp : tm_ori;
+    const int sentinel = (P == 1) ? a.cmp_rows : a.ori_rows;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (ppool[i] < 0 || prow[i] < 0) prow[i] = sentinel;
+    const uint32_t dst = sK + (uint32_t)(32 * h + lane) * 128u;
+    for (int c = kHelperChunk0; c < nchunks; ++c)
+      tma_gather4(dst + c * kChunkBytes, m, c * 64, prow[0], prow[1], prow[2], prow[3], bar);
+  }
+}
+
 // Coalesced store of one warp's 32 rows x 32 bytes: lane i holds row i's
 // 32 bytes in v[0..1].  The rows go through the warp's 1 KB staging buffer
 // (16-byte slot q of row i at slot q ^ ((i >> 2) & 1): conflict-free both
@@ -847,11 +917,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       // written (arming the TMA bytes in TMA mode) and one cp.async
       // completion arrival per lane.
       for (int g = 0; g < kChunkGroups; ++g)
-        mbar_init(smem_addr(&ctl.kv_full[i][g]), kNumProducerWarps + kProducerThreads);
+        mbar_init(smem_addr(&ctl.kv_full[i][g]),
+                  kNumProducerWarps + kProducerThreads + (g == 2 ? kNumHelperWarps : 0));
       mbar_init(smem_addr(&ctl.kv_empty[i]), 1);
       mbar_init(smem_addr(&ctl.s_full[i]), 1);
       mbar_init(smem_addr(&ctl.s_empty[i]), kSoftmaxThreads);
     }
+    for (int h = 0; h < kNumHelperWarps; ++h)
+      for (int i = 0; i < 2; ++i) mbar_init(smem_addr(&ctl.gready[h][i]), 2);
     mbar_init(smem_addr(&ctl.q_full), 1);
     mbar_init(smem_addr(&ctl.q_empty), 1);
     mbar_init(smem_addr(&ctl.p_full), kSoftmaxThreads);
@@ -933,6 +1006,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int cg = 0; cg < kChunkGroups; ++cg) bar[cg] = smem_addr(&ctl.kv_full[stage][cg]);
           const uint32_t sK = sK0 + stage * kStageBytes;
           if (lane == 0) ctl.valid[stage][pw] = (uint16_t)(va_cur & 0xffffu);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_addr(&ctl.gready[pw >> 1][stage]));
           const bool owner = warm && half == new_half && (new_row >> 4) == pw;
           if (owner && lane == 0) {
 #pragma unroll
@@ -1021,8 +1096,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int cg = 0; cg < kChunkGroups; ++cg) bar[cg] = smem_addr(&ctl.kv_full[stage][cg]);
         const uint32_t sK = sK0 + stage * kStageBytes;
         if (lane == 0) ctl.valid[stage][pw] = (uint16_t)(va_cur & 0xffffu);
-        load_tile_rows(args, sa, 0, nchunks, sK, bar, pw, lane, lsu, row_bytes, gran, &tm_ori,
-                       &tm_cmp, &tm_ori16, &tm_cmp16);
+        // The gather helper of this warp pair loads chunks kHelperChunk0.. in
+        // TMA mode; it reads the sources from gsrc once both warps arrived.
+        if (lane < 16) {
+          ctl.gsrc_row[stage][pw * 16 + lane] = sa.row;
+          ctl.gsrc_pool[stage][pw * 16 + lane] = (int8_t)sa.pool;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_addr(&ctl.gready[pw >> 1][stage]));
+        load_tile_rows(args, sa, 0, lsu ? nchunks : min(nchunks, kHelperChunk0), sK, bar, pw,
+                       lane, lsu, row_bytes, gran, &tm_ori, &tm_cmp, &tm_ori16, &tm_cmp16);
 #pragma unroll
         for (int cg = 0; cg < kChunkGroups; ++cg) cp_async_arrive_noinc(bar[cg]);
         if (leader && lane == 0) trace(tr, 0, 3 * produced + 2);
@@ -1031,6 +1114,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     cp_async_wait_all();
+  } else if (warp >= kHelperWarp0 && warp < kHelperWarp0 + kNumHelperWarps) {
+    // ======================= gather helpers =======================
+    // Same tile sequence as the producers: per tile, wait until producer
+    // warps 2h, 2h + 1 have the stage free and its sources in gsrc, then
+    // load chunk group 2 of their rows (plain TMA tiles) or just arrive
+    // (ring rows, cp.async mode: the producers load every chunk).
+    const int h = warp - kHelperWarp0;
+    const bool lsu = (args.gather == kGatherLsu);
+    uint32_t gready_par = 0u;  // bit = stage
+    int stage = 0;
+    bool ok = true;
+    RowStream rs(rows, span.r0, span.r1);
+    for (int r = span.r0; ok && span.r0 >= 0 && r <= span.r1; ++r) {
+      const Row rv = rs.take(r);
+      const int tiles = row_tiles(rv);
+      const int ja = (r == span.r0) ? span.t0 : 0;
+      const int jb = (r == span.r1) ? span.t1 : (tiles > 0 ? tiles : 1);
+      if (tiles == 0 || ja >= jb) continue;
+      const bool ring = (rv.flags & kRowRing) && !lsu && ja == 0 && jb == 2;
+      for (int j = ja; j < jb; ++j) {
+        if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.gready[h][stage],
+                                              (gready_par >> stage) & 1u, err, 3))) {
+          ok = false;
+          break;
+        }
+        gready_par ^= 1u << stage;
+        const uint32_t bar = smem_addr(&ctl.kv_full[stage][2]);
+        if (ring || lsu || nchunks <= kHelperChunk0) {
+          if (lane == 0) mbar_arrive(bar);
+        } else {
+          helper_rows(args, &tm_ori, &tm_cmp, &tm_ori16, &tm_cmp16, ctl.gsrc_row[stage],
+                      ctl.gsrc_pool[stage], h, lane, sK0 + stage * kStageBytes, bar, nchunks);
+        }
+        stage ^= 1;
+      }
+    }
   } else if (warp == kQWarp) {
     // ======================= Q loader =======================
     // Q of a row (64 heads of this group, one 64 x 64 TMA box per chunk) is
