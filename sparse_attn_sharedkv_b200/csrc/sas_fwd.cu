@@ -279,6 +279,16 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -1388,25 +1398,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     // tiles back freed its K stage) and PV k+2 is not yet released, so
     // kv_empty[k % 2] is exactly one phase short of or at the awaited
     // completion and the parity test is exact.
-    auto wait_pv = [&](int k, int site) -> bool {
-      return wait_bar(&ctl, &ctl.kv_empty[k & 1], (uint32_t)((k >> 1) & 1), err, site);
-    };
+
     uint32_t xph = 0u;  // bit = exchange barrier
     int stage = 0, sbuf = 0, xpar = 0;
     // Partner exchange through ctl.red[xpar], ordered by the bounded
     // mbarrier ctl.xbar[xpar] (all 128 softmax threads arrive, then wait).
-    auto exchange = [&](int site) -> bool {
-      mbar_arrive(smem_addr(&ctl.xbar[xpar]));
-      const bool w = wait_bar(&ctl, &ctl.xbar[xpar], (xph >> xpar) & 1u, err, site);
-      xph ^= 1u << xpar;
-      return w;
-    };
+
     bool ok = true;
     const int dv = args.head_dim_v;
 
-    RowStream rs(rows, span.r0, span.r1);
     for (int r = span.r0; ok && span.r0 >= 0 && r <= span.r1; ++r) {
-      const Row rv = rs.take(r);
+      // (loaded at the row start, not prefetched: the softmax's registers go
+      // to the score tile)
+      const Row rv = load_row(rows, r);
       const int tiles = row_tiles(rv);
       const int ja = (r == span.r0) ? span.t0 : 0;
       const int jb = (r == span.r1) ? span.t1 : (tiles > 0 ? tiles : 1);
@@ -1470,7 +1474,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           mx = fmaxf(mx, v);
         }
         ctl.red[xpar][half][m] = mx;
-        if (!__all_sync(0xffffffffu, exchange(34))) { ok = false; break; }
+        mbar_arrive(smem_addr(&ctl.xbar[xpar]));
+        const bool xw = wait_bar(&ctl, &ctl.xbar[xpar], (xph >> xpar) & 1u, err, 34);
+        xph ^= 1u << xpar;
+        if (!__all_sync(0xffffffffu, xw)) { ok = false; break; }
         mx = fmaxf(mx, ctl.red[xpar][half ^ 1][m]);
         xpar ^= 1;
         if (threadIdx.x == 0) trace(tr, 2, 4 * pv_count + 1);
@@ -1484,39 +1491,45 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
         float lsum = 0.f;
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float p0 = exp2f(x[i] - m_use);
-          const float p1 = exp2f(x[i + 1] - m_use);
-          lsum += p0 + p1;
-          pk[i / 2] = pack2<kBf16>(p0, p1);
-        }
-        l_run += lsum;
-        // P(j) into chunk 8 of tile j's own stage (free: S(j) is complete).
+        // P(j) into chunk 8 of tile j's own stage (free: S(j) is complete),
+        // one 16-byte granule (8 keys) at a time.
         uint8_t* prow = gbase + kSmemK0 + st * kStageBytes + kPChunk * kChunkBytes;
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
-          uint4 v = make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
-          *reinterpret_cast<uint4*>(prow + swz(m, 4 * half + g)) = v;
+          uint32_t pk[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int i = 8 * g + 2 * q;
+            const float p0 = exp2f(x[i] - m_use);
+            const float p1 = exp2f(x[i + 1] - m_use);
+            lsum += p0 + p1;
+            pk[q] = pack2<kBf16>(p0, p1);
+          }
+          *reinterpret_cast<uint4*>(prow + swz(m, 4 * half + g)) =
+              make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
+        l_run += lsum;
         fence_proxy_async();
         // The running max moved by more than the lazy threshold: O must be
         // rescaled after PV(j-1) (number pv_count - 1) and before PV(j).
         if (j > ja && __any_sync(0xffffffffu, rescale)) {
-          if (!__all_sync(0xffffffffu, wait_pv(pv_count - 1, 32))) {
+          const int kp = pv_count - 1;  // PV(j-1): phase kp / 2 of kv_empty[kp % 2]
+          if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.kv_empty[kp & 1],
+                                                (uint32_t)((kp >> 1) & 1), err, 32))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          for (int c = 0; c < 8; ++c) {
-            const uint32_t ta = tmem + lane_off + kTmemO + 32u * c;
-            uint32_t v[32];
-            tmem_ld32(ta, v);
+          // 16 columns at a time (a rare path; keeps the softmax's registers low)
+#pragma unroll 1
+          for (int c = 0; c < 16; ++c) {
+            const uint32_t ta = tmem + lane_off + kTmemO + 16u * c;
+            uint32_t v[16];
+            tmem_ld16(ta, v);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-            tmem_st32(ta, v);
+            for (int i = 0; i < 16; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+            tmem_st16(ta, v);
           }
           tmem_wait_st();
         }
