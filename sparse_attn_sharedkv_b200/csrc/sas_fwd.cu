@@ -1210,6 +1210,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t q_full_par = 0u, p_full_par = 0u, o_free_par = 1u;
       int pv_issued = 0, qk_issued = 0, q_seen = 0;
       bool ok = true;
+      // Shared memory the MMAs read is written by TMA (async proxy) or by the
+      // softmax threads, which fence it to the async proxy before arriving on
+      // p_full, so this thread needs no proxy fence of its own.
       // The worker's tiles form one stream across rows; tile t uses K stage
       // t % 2 and S buffer t % 2.  QKs and PVs are issued as two independent
       // in-order streams, each step as soon as its inputs are in: PV(t)
@@ -1243,7 +1246,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (p_ok && o_ok) {
             trace(tr, 1, 4 * pv_issued + 2);
-            fence_proxy_async();
             tc_fence_after();
             issue_pv(tmem + kTmemO, sK0 + pstage * kStageBytes, idesc_pv, pc.first());
             trace(tr, 1, 4 * pv_issued + 3);
@@ -1278,7 +1280,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (s_ok &&
               mbar_test(smem_addr(&ctl.kv_full[qstage][qg]), (kv_full_par >> qstage) & 1u)) {
             trace(tr, 3, 2048 + 3 * qk_issued + qg);
-            fence_proxy_async();
             tc_fence_after();
             issue_qk_group<nchunks>(tmem + kTmemS + 128u * qstage, sQ,
                                     sK0 + qstage * kStageBytes, idesc_qk, qg);
