@@ -69,7 +69,7 @@ constexpr int kNumHelperWarps = 2;
 constexpr int kHelperChunk0 = 6;
 constexpr int kEpiWarp0 = 12;      // epilogue warps 12..15 (TMEM lane quarters 0..3)
 constexpr int kNumEpiWarps = 4;
-constexpr int kThreads = 32 * 16;  // warps 10, 11 have no role
+constexpr int kThreads = 32 * 16;
 constexpr int kEpiThreads = 32 * kNumEpiWarps;
 constexpr int kSoftmaxThreads = 32 * kNumSoftmaxWarps;
 constexpr int kProducerThreads = 32 * kNumProducerWarps;
@@ -92,8 +92,10 @@ constexpr int kSmemDynamic = kSmemTiles + 1024;        // + runtime 1 KB alignme
 // that chunk holds dims 512..575, which only QK reads (V is dims 0..511), so
 // it is free once S(j) is complete and is double-buffered with the stages.
 constexpr int kPChunk = 8;
-constexpr int kGatherLsu = 0;  // key rows by cp.async 16 B from the 4 producer warps
-constexpr int kGatherTma = 1;  // key rows by TMA tile::gather4 from the 4 producer warps
+// FwdArgs::gather: key rows by cp.async 16 B from the four producer warps
+// (kGatherLsu), or (any other value) by TMA boxes and tile::gather4 from the
+// producers and the gather helpers.
+constexpr int kGatherLsu = 0;
 
 // TMEM columns.
 constexpr uint32_t kTmemCols = 512;
@@ -186,15 +188,6 @@ __device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int x, i
                : "memory");
 }
 
-__device__ __forceinline__ void tma_prefetch_gather4(const CUtensorMap* map, int x, int y0, int y1,
-                                                     int y2, int y3) {
-  asm volatile(
-      "cp.async.bulk.prefetch.tensor.2d.L2.global.tile::gather4 [%0, {%1, %2, %3, %4, %5}];" ::"l"(
-          reinterpret_cast<uint64_t>(map)),
-      "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3)
-      : "memory");
-}
-
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
                "r"(src_bytes)
@@ -263,19 +256,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
         "=r"(r[14]), "=r"(r[15])
       : "r"(taddr)
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
-      "%28, %29, %30, %31, %32};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
-      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
-      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
-      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
-      "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
 
