@@ -217,3 +217,22 @@ def test_device_error_word_on_bad_block_table():
     out = sparse_attn_sharedkv(case.q, **case.kwargs())
     torch.cuda.synchronize()
     assert torch.isfinite(out.float()).all()
+
+
+@pytest.mark.parametrize("kw", [
+    dict(seed=91, layout_q="TND", scenario=3, idx_mode="dirty", K=200, q_lens=(5, 3),
+         kv_lens=(900, 700)),
+    dict(seed=92, layout_q="TND", scenario=2, ratio=8, q_lens=(6, 2), kv_lens=(1400, 600),
+         H=128),
+    dict(seed=93, layout_q="BSND", B=2, scenario=3, q_lens=(3, 1), kv_lens=(300, 40), K=64,
+         D=512, d_v=None),
+])
+def test_cp_async_gather_mode(kw, monkeypatch):
+    # SAS_GATHER=lsu: the producers move whole key rows by cp.async (no TMA,
+    # the gather helpers only arrive); same results as the TMA path's gate.
+    case = W.random_case(**kw)
+    monkeypatch.setenv("SAS_GATHER", "lsu")
+    out, lse = run(case, num_sms=37)
+    ex, gold, o_lse = oracle(case)
+    check_north_star(out, ex, gold)
+    check_lse_tight(lse, o_lse)
