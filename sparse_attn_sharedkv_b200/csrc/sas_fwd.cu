@@ -317,9 +317,10 @@ struct Ctl {
   uint16_t valid[2][4];          // per stage: slot bits of keys 16w..16w+15
   float red[2][2][kHeadsPerCta];  // [parity][half][row]: partner exchange
   // Final statistics of a (row, piece), softmax -> epilogue warps, double-
-  // buffered by the parity of the piece's ordinal (the epilogue of piece k
-  // releases o_free before any PV, hence any QK, of piece k + 2 can start).
+  // buffered by the parity of the piece's ordinal k: the softmax writes
+  // buffer k % 2 once the epilogue has read piece k - 2 from it (fin_free).
   uint64_t fin_full[2];
+  uint64_t fin_free[2];
   uint64_t o_full;                  // O of a (row, piece) complete (last PV committed)
   float fin_m[2][kHeadsPerCta];     // running max (log2 domain)
   float fin_l[2][2][kHeadsPerCta];  // [parity][half][head] partial row sums
@@ -925,6 +926,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(smem_addr(&ctl.xbar[1]), kSoftmaxThreads);
     mbar_init(smem_addr(&ctl.fin_full[0]), kSoftmaxThreads);
     mbar_init(smem_addr(&ctl.fin_full[1]), kSoftmaxThreads);
+    mbar_init(smem_addr(&ctl.fin_free[0]), kEpiThreads);
+    mbar_init(smem_addr(&ctl.fin_free[1]), kEpiThreads);
     ctl.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -1334,6 +1337,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ew == 0 && lane == 0) trace(tr, 3, 3 * k + 1);
       const float m_run = ctl.fin_m[fp][m];
       const float l_tot = ctl.fin_l[fp][0][m] + ctl.fin_l[fp][1][m];
+      mbar_arrive(smem_addr(&ctl.fin_free[fp]));  // statistics read: the buffer is free
       const float inv = (l_tot > 0.f) ? 1.f / l_tot : 0.f;
       const float lse = (m_run + log2f(l_tot)) * kLn2;
       const bool split = rv.partial_base >= 0;
@@ -1523,6 +1527,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- hand this (row, piece)'s statistics to the epilogue (producer
       // warps); m_run is identical in both key halves ----
       const int fp = rows_done & 1;
+      // The epilogue has read piece rows_done - 2 from this buffer (phase
+      // rows_done / 2 - 1 of fin_free[fp]; the first use passes at once).
+      if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.fin_free[fp],
+                                            (uint32_t)(((rows_done >> 1) & 1) ^ 1), err, 35)))
+        break;
       if (half == 0) ctl.fin_m[fp][m] = m_run;
       ctl.fin_l[fp][half][m] = l_run;
       mbar_arrive(smem_addr(&ctl.fin_full[fp]));
