@@ -307,7 +307,11 @@ struct Ctl {
   uint64_t q_full, q_empty;
   uint64_t s_full[2];
   uint64_t s_empty[2];
-  uint64_t p_full, o_free, drain;
+  // P(t) written: phase t / 2 of p_full[t % 2].  Two barriers, so that the
+  // softmax can never complete two phases of one before its consumer tested
+  // the first (P(t + 2) needs S(t + 2), which needs PV(t) issued).
+  uint64_t p_full[2];
+  uint64_t o_free, drain;
   uint64_t xbar[2];               // softmax partner exchange (bounded, no bar.sync)
   uint64_t gready[kNumHelperWarps][2];  // [helper][stage]: the tile's sources are in gsrc
   int32_t gsrc_row[2][kTileKeys];       // [stage][slot]: source row of each key slot
@@ -918,7 +922,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; i < 2; ++i) mbar_init(smem_addr(&ctl.gready[h][i]), 2);
     mbar_init(smem_addr(&ctl.q_full), 1);
     mbar_init(smem_addr(&ctl.q_empty), 1);
-    mbar_init(smem_addr(&ctl.p_full), kSoftmaxThreads);
+    mbar_init(smem_addr(&ctl.p_full[0]), kSoftmaxThreads);
+    mbar_init(smem_addr(&ctl.p_full[1]), kSoftmaxThreads);
     mbar_init(smem_addr(&ctl.o_free), kEpiThreads);
     mbar_init(smem_addr(&ctl.o_full), 1);
     mbar_init(smem_addr(&ctl.drain), 1);
@@ -1215,9 +1220,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool progress = false;
         // ---- PV of the oldest tile whose QK is issued ----
         if (pending > 0) {
-          if (!p_ok && mbar_test(smem_addr(&ctl.p_full), p_full_par)) {
+          if (!p_ok && mbar_test(smem_addr(&ctl.p_full[pstage]), (p_full_par >> pstage) & 1u)) {
             p_ok = true;
-            p_full_par ^= 1u;
+            p_full_par ^= 1u << pstage;
           }
           if (!o_ok) {
             if (!pc.first()) {
@@ -1520,7 +1525,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_before();
         if (threadIdx.x == 0) trace(tr, 2, 4 * pv_count + 2);
-        mbar_arrive(smem_addr(&ctl.p_full));
+        mbar_arrive(smem_addr(&ctl.p_full[st]));
         ++pv_count;
       }
       if (!ok) break;
