@@ -2,6 +2,7 @@
 """Benchmark of the sparse shared-KV attention forward on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl reference]
+                    [--comparator flashmla]
 
 One step = one call of the hot path (``sparse_attn_sharedkv``: plan reuse,
 tcgen05 attention kernel, split-KV combine) over one batch of the workload.
@@ -19,6 +20,11 @@ Printed JSON line (rank 0):
   algorithmic bytes (or FLOPs) per launch / duration vs the measured peak;
 * ``cpu_baseline``: the CPU oracle (a port of the reference's golden
   attention) timed on this host on a bounded sample of the same workload.
+
+``--comparator flashmla`` (configs 3 and 4) adds ``comparator``: vLLM's
+FlashMLA sparse kernel, a library kernel, timed on the same inputs through its
+Python wrapper, with the largest output difference — a yardstick, not part
+of ``value``.
 
 ``--impl reference`` times that CPU implementation alone (the reference's
 own implementation cannot run here: it needs an Ascend NPU / TileLang-Ascend;
@@ -478,12 +484,65 @@ def run_gpu(args):
             "clocks": clocks,
             "gpu_launches": launches_per_step * args.steps,
         }
+        if args.comparator == "flashmla":
+            line["comparator"] = flashmla_comparator(A, case, kw)
         print(json.dumps(line), flush=True)
     if ws > 1:
         import torch.distributed as dist
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def flashmla_comparator(A, case, kw, reps: int = 20):
+    """Optional yardstick (``--comparator flashmla``): vLLM's FlashMLA sparse
+    prefill kernel (a library kernel, run through its Python wrapper) on the
+    same inputs, for the pure top-k workloads it supports (configs 3 and 4:
+    sinks -inf, no window).  The paged cache is viewed as one flat key array
+    and each top-k position is translated to its pool row through the block
+    table.  Returns its median kernel time and the largest output difference."""
+    import torch
+    try:
+        from vllm.third_party.flashmla.flash_mla_interface import flash_mla_sparse_fwd
+    except Exception as e:  # library absent or not built for this GPU
+        return {"unavailable": f"vLLM FlashMLA not importable: {type(e).__name__}"}
+    if case.cmp_sparse_indices is None or case.ori_win_left != -1 or case.q.shape[-2] % 64:
+        return {"unavailable": "FlashMLA sparse covers pure top-k with 64k heads only"}
+    q = case.q
+    H = q.shape[-2]
+    qf = q.reshape(-1, H, q.shape[-1]).contiguous()
+    pool, table = case.cmp_kv, case.cmp_block_table
+    bs = pool.shape[1]
+    kvf = pool.reshape(-1, 1, pool.shape[-1])
+    K = case.cmp_sparse_indices.shape[-1]
+    idx = case.cmp_sparse_indices.reshape(-1, K).long()
+    if case.layout_q == "TND":
+        cu = case.cu_seqlens_q.long()
+        bt = torch.repeat_interleave(torch.arange(len(cu) - 1, device=q.device), cu[1:] - cu[:-1])
+    else:
+        bt = torch.arange(q.shape[0], device=q.device).repeat_interleave(q.shape[1])
+    pos = idx.clamp(min=0)
+    rows = table.long()[bt[:, None], pos // bs] * bs + pos % bs
+    rows = torch.where(idx >= 0, rows, torch.full_like(rows, -1))
+    rows = rows.to(torch.int32).view(-1, 1, K).contiguous()
+    run = lambda: flash_mla_sparse_fwd(qf, kvf, rows, case.softmax_scale, 512)
+    out_fm = run()[0]
+    ours = A.sparse_attn_sharedkv(q, **kw).reshape(-1, H, 512)
+    diff = (ours.float() - out_fm.float()).abs().max().item()
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize()
+    times = []
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(reps):
+        s.record()
+        run()
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    times.sort()
+    return {"impl": "vLLM FlashMLA flash_mla_sparse_fwd (library kernel, same inputs)",
+            "kernel_ms": times[len(times) // 2], "max_abs_diff_out": diff}
 
 
 def _rebuild_call(A, case, kw):
@@ -524,6 +583,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--comparator", default=None, choices=["flashmla"],
+                    help="also time vLLM's FlashMLA sparse kernel on the same inputs "
+                         "(configs 3 and 4; informational, not part of value)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
