@@ -99,6 +99,23 @@ SAS_HD inline QueryKeys query_keys(int32_t scenario, int32_t act_q, int32_t act_
   return k;
 }
 
+// Cost axis of the work plan (both planners): 1 unit per row (Q load,
+// epilogue) + 1 per 64-key tile.  Rows of at most kSnapTiles key tiles are
+// never split between workers: all their units take the row's midpoint, so
+// the worker whose share holds that point runs the whole row (no fp32
+// partials to write and combine, and ring rows stay on the warm path).
+// Longer rows are cut at tile granularity.
+constexpr int64_t kSnapTiles = 4;
+
+// Point of unit j of a row that starts at `start` on the cost axis and has
+// `tiles` key tiles, doubled to stay integral; a row without tiles is one
+// unit.
+SAS_HD inline int64_t unit_mid2(int64_t start, int64_t tiles, int64_t j) {
+  if (tiles <= 0) return 2 * start + 1;
+  if (tiles <= kSnapTiles) return 2 * start + 1 + tiles;
+  return 2 * (start + 1 + j) + 1;
+}
+
 // Windows of 65..128 keys with no compressed branch run as ring rows.
 SAS_HD inline bool ring_window(int32_t scenario, int32_t win_left) {
   return scenario == SAS_SCENARIO_SWA && win_left >= 64 && win_left < kRingKeys;

@@ -8,7 +8,7 @@
 // `window + compressed` key slots (golden.py:125-150); rows are laid out in
 // token order on a cost axis (a fixed per-row cost for the Q load and output
 // store, plus one unit per 64-key tile) and cut into `num_workers` equal
-// spans at tile granularity.  A row whose tiles land on several workers is a
+// spans at tile granularity (rows of at most sas::kSnapTiles tiles whole).  A row whose tiles land on several workers is a
 // split row: each worker writes an fp32 partial (normalised O + LSE) and the
 // combine kernel merges them (the flash-decode reduction the reference plans
 // but never runs).
@@ -24,7 +24,7 @@ namespace {
 
 using sas::kRowInts;
 
-constexpr int64_t kRowCost = 1;   // Q load + epilogue, in tile units
+constexpr int64_t kRowCost = 1;   // Q load + epilogue, in tile units (sas::unit_mid2)
 constexpr int64_t kTileCost = 1;
 
 struct Row {
@@ -111,8 +111,7 @@ int build(const SasProblem& p, int32_t num_sms, bool fill, Built* out) {
     int64_t units = tiles[r] > 0 ? tiles[r] : 1;
     int64_t w_first = -1, w_last = -1, pieces = 0;
     for (int64_t j = 0; j < units; ++j) {
-      int64_t mid2 = tiles[r] > 0 ? 2 * (start[r] + kRowCost + j * kTileCost) + kTileCost
-                                  : 2 * start[r] + kRowCost;
+      const int64_t mid2 = sas::unit_mid2(start[r], tiles[r], j);
       int64_t w = owner(mid2);
       if (w_first < 0) w_first = w;
       if (w != w_last) {

@@ -6,7 +6,7 @@
 // Same rows, workers, split rows and partial bases as the host planner for
 // the same lengths (rows carry the same key bounds; the cost axis is 1 per
 // row + 1 per 64-key tile; the owner of a unit is the worker whose share of
-// the cost axis holds the unit's midpoint).  Only the section offsets differ:
+// the cost axis holds the unit's midpoint, sas::unit_mid2).  Only the section offsets differ:
 // they are fixed by host-known bounds (rows = total_tokens, split rows <=
 // workers - 1, partial slots <= 2 (workers - 1)); the unused split entries
 // carry zero pieces.
@@ -82,11 +82,7 @@ __device__ __forceinline__ int64_t owner_of(int64_t mid2, int64_t nw, int64_t to
   return w >= nw ? nw - 1 : w;
 }
 
-// Midpoint (doubled) of unit j of a row starting at `start` with `tiles`
-// tiles (a row without tiles is one unit of cost kRowCost).
-__device__ __forceinline__ int64_t unit_mid2(int64_t start, int64_t tiles, int64_t j) {
-  return tiles > 0 ? 2 * (start + kRowCost + j * kTileCost) + kTileCost : 2 * start + kRowCost;
-}
+using sas::unit_mid2;
 
 __device__ void record(int32_t* err, int detail) {
   if (err != nullptr && atomicCAS(err, 0, SAS_ERR_DEVICE) == 0) {

@@ -105,6 +105,8 @@ def test_plan_covers_every_tile_once(case, sms):
         assert all((r, j) in seen for j in range(units)), r
         ws = [w for w, _ in pieces[r]]
         assert ws == sorted(ws) and len(set(ws)) == len(ws)
+        if units <= 4:
+            assert len(ws) == 1, r  # rows of at most 4 tiles run whole on one worker
         assert [pc for _, pc in pieces[r]] == list(range(len(ws)))  # piece ordinals
         assert row[5] == ws[0]
         if len(ws) > 1:
