@@ -6,20 +6,26 @@
 
 One step = one call of the hot path (``sparse_attn_sharedkv``: plan reuse,
 tcgen05 attention kernel, split-KV combine) over one batch of the workload.
-The default workload is the benchmark's second configuration (SWA prefill,
-TND, 4 sequences of 512..4096 tokens, 64 heads, d_qk 576 / d_v 512, window
-128, paged block 64); ``--config 1..5`` selects any of the five.
+The default workload is the benchmark's fourth configuration, the largest
+that runs on one GPU (sparse prefill, TND, 8 sequences of 4096 tokens,
+128 heads, top-k 2048 causal indices, d_qk 576 / d_v 512, paged block 64);
+``--config 1..5`` selects any of the five.
 
 Printed JSON line (rank 0):
 * ``value``: whole-job algorithmic TFLOP/s with inputs resident in HBM
-  (N ranks x FLOPs per step x K / max over ranks of the device time);
+  (FLOPs of the call x K / max over ranks of the device time);
 * ``e2e``: the same metric through the public API with host buffers: every
   step copies its inputs (q, indices, block tables) from pinned host memory
-  and reads the LSE back; the KV caches stay resident, as in serving;
+  and copies the output and the LSE back into pinned host memory; the KV
+  caches stay resident, as in serving; steps are pipelined over three
+  streams (copy-in, call, copy-out);
 * ``roofline``: the attention kernel alone (CUDA events on its stream),
   algorithmic bytes (or FLOPs) per launch / duration vs the measured peak;
+* ``per_config`` (N = 1): kernel and call times with their roofline
+  fractions for the other four configurations, same process and GPU;
 * ``cpu_baseline``: the CPU oracle (a port of the reference's golden
-  attention) timed on this host on a bounded sample of the same workload.
+  attention) timed on this host on a bounded sample of the same workload,
+  with the threads it used and the host's core count.
 
 ``--comparator flashmla`` (configs 3 and 4) adds ``comparator``: vLLM's
 FlashMLA sparse kernel, a library kernel, timed on the same inputs through its
@@ -30,11 +36,13 @@ of ``value``.
 own implementation cannot run here: it needs an Ascend NPU / TileLang-Ascend;
 its CPU golden cannot travel to the GPU box, so the oracle port stands in).
 
-Multi-GPU (torchrun, one rank per GPU): the global workload is N copies of
-the configuration's sequences, sharded one copy per rank (weak scaling; the
-step itself needs no collective).  The sharded call's one exchange, the
-all-gather of the output / LSE shards (sharding.gather_outputs, NCCL), is
-timed separately under ``allgather``.
+Multi-GPU (torchrun, one rank per GPU): the configuration's call is split
+over the N ranks (sharding.plan_shards: decode by batch, TND prefill by
+token ranges, each rank holding only the KV pages its rows reach), so the
+total work is fixed (strong scaling); ``value`` and ``e2e`` take the max over
+ranks.  The sharded call's one exchange, a gather of the output / LSE shards
+to rank 0 over NCCL, is timed separately under ``gather``; in ``e2e`` every
+rank copies its own output shard to host memory.
 """
 
 from __future__ import annotations
@@ -244,14 +252,24 @@ def dist_env():
     return ws, rank, local
 
 
+def cpu_threads():
+    """(threads the CPU oracle uses, host cores)."""
+    host = os.cpu_count() or 1
+    try:
+        from threadpoolctl import threadpool_info
+        used = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    except Exception:
+        used = host
+    return used, host
+
+
 def run_reference(args):
     """The CPU implementation of the path (oracle port of golden.py) alone."""
     ws, rank, _ = dist_env()
     if rank != 0:
         return 0
-    import torch
 
-    from sparse_attn_sharedkv_b200 import workloads as W
+    from tests import workloads as W
 
     case = W.baseline_case(args.config - 1, device="cpu")
     flops_tok = per_token_flops(case)
@@ -264,14 +282,17 @@ def run_reference(args):
             vals.append(f / s / 1e12)
             samples.append(t)
     value = statistics.median(vals) if vals else 0.0
+    _, host = cpu_threads()
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": None, "higher_is_better": True,
+        "scaling": "strong" if args.gpus > 1 else "weak",
         "vs_baseline": None, "dtype": "f32 (bf16 inputs)", "data": "synthetic",
         "impl": "reference",
         "config": {"workload": W.BASELINE_NAMES[args.config - 1], "device": "cpu"},
-        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads,
+                         "host_cores": host, "kind": "port",
                          "sample": f"{int(statistics.median(samples))} query tokens per step "
                                    f"(~{budget:.0f} s of CPU work each), random tokens"},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
@@ -281,7 +302,198 @@ def run_reference(args):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# Workloads on the GPU.
+# ---------------------------------------------------------------------------
+
+def host_lengths(kw):
+    """Lengths on the host (the reference reads them with .cpu() anyway)."""
+    kw = dict(kw)
+    kw["seqused_kv"] = kw["seqused_kv"].cpu()
+    if kw.get("cu_seqlens_q") is not None:
+        kw["cu_seqlens_q"] = kw["cu_seqlens_q"].cpu()
+    return kw
+
+
+def shard_case(W, full, q, kw):
+    """A Case for a shard's (q, kwargs), for the work accounting."""
+    return W.Case(full.name, full.layout_q, q, kw["ori_kv"], kw["ori_block_table"],
+                  torch_tensor(kw["seqused_kv"]), full.sinks, full.softmax_scale,
+                  cu_seqlens_q=(torch_tensor(kw["cu_seqlens_q"])
+                                if kw.get("cu_seqlens_q") is not None else None),
+                  cmp_kv=kw.get("cmp_kv"), cmp_block_table=kw.get("cmp_block_table"),
+                  cmp_sparse_indices=kw.get("cmp_sparse_indices"),
+                  cmp_ratio=full.cmp_ratio, ori_win_left=full.ori_win_left,
+                  head_dim_v=full.head_dim_v)
+
+
+def torch_tensor(x):
+    import torch
+    return torch.as_tensor(x)
+
+
+def kernel_alone_ms(A, q, kw, steps, flush, stream):
+    """Mean device time of the attention kernel alone (sas_fwd_execute with
+    the attention phase only, on the call's cached plan), CUDA events on the
+    launching stream."""
+    import ctypes as C
+
+    import torch
+
+    from sparse_attn_sharedkv_b200 import _lib
+    prob, fp, keep = _rebuild_call(A, q, kw)
+    hit = None
+    for v in A._PLAN_CACHE.values():
+        hit = v
+    ws_t, nbytes, pinfo = hit
+    L = _lib.lib()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps)]
+    for i in range(steps):
+        if flush is not None:
+            flush.zero_()
+        evs[i][0].record(stream)
+        _lib.check("sas_fwd_execute",
+                   L.sas_fwd_execute(C.byref(prob), C.byref(fp), C.byref(pinfo), ws_t.data_ptr(),
+                                     nbytes, C.c_void_p(stream.cuda_stream), _lib.PHASE_ATTN))
+        evs[i][1].record(stream)
+    torch.cuda.synchronize()
+    del keep
+    return statistics.mean(a.elapsed_time(b) for a, b in evs)
+
+
+def step_times_ms(A, q, kw, steps, flush, stream, sampler=None):
+    """Device time of each of `steps` full calls (plan reuse, attention,
+    combine), CUDA events on the launching stream."""
+    import contextlib
+
+    import torch
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps)]
+    with (sampler if sampler is not None else contextlib.nullcontext()):
+        for i in range(steps):
+            if flush is not None:
+                flush.zero_()
+            evs[i][0].record(stream)
+            A.sparse_attn_sharedkv(q, return_softmax_lse=True, **kw)
+            evs[i][1].record(stream)
+        torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in evs]
+
+
+def roofline(acct, kern_ms, peaks):
+    flops, nbytes = acct["flops"], acct["bytes"]
+    ridge = peaks["bf16_tflops"] * 1e12 / (peaks["hbm_gbs"] * 1e9)
+    if flops / nbytes < ridge:
+        ach = nbytes / (kern_ms * 1e-3) / 1e9
+        return "hbm", ach, peaks["hbm_gbs"], "GB/s"
+    ach = flops / (kern_ms * 1e-3) / 1e12
+    return "tensor", ach, peaks["bf16_tflops"], "TFLOP/s"
+
+
+def e2e_pipelined(A, q, kw, n_steps, dev):
+    """End to end through the public API with host buffers: every step copies
+    its inputs (q, indices, block tables) from pinned host memory, runs the
+    call and copies the output and the LSE back into pinned host memory.
+    Steps are pipelined over three streams (copy-in of step i + 1 and
+    copy-out of step i - 1 overlap the call of step i; PCIe is full duplex).
+    Returns (ms per step, h2d bytes per step, d2h bytes per step)."""
+    import torch
+
+    names = ["q"] + [n for n in ("cmp_sparse_indices", "ori_block_table", "cmp_block_table")
+                     if isinstance(kw.get(n), torch.Tensor) and kw[n].is_cuda]
+    src = {"q": q}
+    src.update({n: kw[n] for n in names if n != "q"})
+    host = {n: t.cpu().pin_memory() for n, t in src.items()}
+    bufs = [{n: torch.empty_like(t) for n, t in src.items()} for _ in range(2)]
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    s_in, s_run, s_out = (torch.cuda.Stream(dev) for _ in range(3))
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_run = [torch.cuda.Event() for _ in range(2)]
+    out_host = lse_host = None
+
+    def one(i):
+        nonlocal out_host, lse_host
+        s = i % 2
+        with torch.cuda.stream(s_in):
+            if i >= 2:
+                s_in.wait_event(ev_run[s])  # the call two steps back read bufs[s]
+            for n, t in host.items():
+                bufs[s][n].copy_(t, non_blocking=True)
+            ev_in[s].record(s_in)
+        with torch.cuda.stream(s_run):
+            s_run.wait_event(ev_in[s])
+            kw2 = dict(kw)
+            for n in names:
+                if n != "q":
+                    kw2[n] = bufs[s][n]
+            out, lse = A.sparse_attn_sharedkv(bufs[s]["q"], return_softmax_lse=True, **kw2)
+            ev_run[s].record(s_run)
+        if out_host is None:
+            out_host = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+            lse_host = torch.empty(lse.shape, dtype=lse.dtype, pin_memory=True)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_run[s])
+            out_host.copy_(out, non_blocking=True)
+            lse_host.copy_(lse, non_blocking=True)
+            out.record_stream(s_out)
+            lse.record_stream(s_out)
+
+    one(0)  # warm-up: plans for the run stream, pinned output buffers
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s_in)
+    for i in range(n_steps):
+        one(i)
+    e1.record(s_out)
+    torch.cuda.synchronize()
+    d2h = out_host.numel() * out_host.element_size() + lse_host.numel() * 4
+    ms = e0.elapsed_time(e1) / n_steps
+    return ms, h2d, d2h
+
+
+def other_configs(A, W, cfgs, dev, stream, peaks, steps):
+    """Per-configuration kernel and step times of the workloads other than the
+    headline one, on this GPU, in this process (same clock sampler context)."""
+    import gc
+
+    import torch
+    res = {}
+    for cfg in cfgs:
+        case = W.baseline_case(cfg, device=dev)
+        acct = W.accounting(case)
+        kw = host_lengths(case.kwargs())
+        in_l2 = acct["bytes"] < 2 * L2_BYTES
+        flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev) if in_l2 else None
+        for _ in range(3):
+            A.sparse_attn_sharedkv(case.q, return_softmax_lse=True, **kw)
+        torch.cuda.synchronize()
+        n = max(5, steps)
+        st = step_times_ms(A, case.q, kw, n, flush, stream)
+        kms = kernel_alone_ms(A, case.q, kw, n, flush, stream)
+        bound, ach, peak, unit = roofline(acct, kms, peaks)
+        info = A.last_plan_info
+        res[W.BASELINE_NAMES[cfg]] = {
+            "us_per_call": statistics.mean(st) * 1e3, "kernel_us": kms * 1e3,
+            "tflops": acct["flops"] / (kms * 1e-3) / 1e12,
+            "hbm_gbs": acct["bytes"] / (kms * 1e-3) / 1e9,
+            "roofline": {"bound": bound, "achieved": ach, "peak": peak, "unit": unit,
+                         "frac": ach / peak},
+            "flops": acct["flops"], "bytes": acct["bytes"],
+            "plan": {"workers": info.num_workers, "head_groups": info.head_groups,
+                     "split_rows": info.num_split_rows, "tiles": int(info.total_tiles)},
+            "l2": "flushed between steps" if in_l2 else "inputs larger than L2",
+        }
+        del case, kw, flush
+        A._PLAN_CACHE.clear()
+        gc.collect()
+        torch.cuda.empty_cache()
+    return res
+
+
 def run_gpu(args):
+    import gc
+
     import torch
 
     ws, rank, local = dist_env()
@@ -295,22 +507,30 @@ def run_gpu(args):
                                 device_id=dev)
 
     from sparse_attn_sharedkv_b200 import api as A
-    from sparse_attn_sharedkv_b200 import workloads as W
+    from sparse_attn_sharedkv_b200 import sharding as SH
+    from tests import workloads as W
 
     cfg = args.config - 1
-    case = W.baseline_case(cfg, device=dev)
-    acct = W.accounting(case)
-    kw = case.kwargs()
-    # Lengths live on the host (the reference reads them with .cpu() anyway).
-    kw["seqused_kv"] = case.seqused_kv.cpu()
-    if case.cu_seqlens_q is not None:
-        kw["cu_seqlens_q"] = case.cu_seqlens_q.cpu()
-    q = case.q
-    in_l2 = acct["bytes"] < 2 * L2_BYTES
+    full = W.baseline_case(cfg, device=dev)
+    acct_full = W.accounting(full)
+    kw_full = host_lengths(full.kwargs())
+    if ws > 1:
+        # The north-star split: one call's rows partitioned over the ranks
+        # (decode by batch, TND prefill by token ranges), each rank holding
+        # only the KV pages its rows reach; total work fixed (strong scaling).
+        bounds = SH.plan_shards(full.q, full.kwargs(), ws)
+        sh = SH.make_shard(full.q, full.kwargs(), bounds[rank], rank, compact_pages=True)
+        if sh.empty:
+            q, kw, acct = None, None, dict(flops=0.0, bytes=1, tokens=0)
+        else:
+            q, kw = sh.q.contiguous(), host_lengths(sh.kwargs)
+            acct = W.accounting(shard_case(W, full, q, sh.kwargs))
+    else:
+        bounds = [(0, 0)]
+        q, kw, acct = full.q, kw_full, acct_full
+    in_l2 = acct_full["bytes"] / ws < 2 * L2_BYTES
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev) if in_l2 else None
-
-    def step():
-        return A.sparse_attn_sharedkv(q, return_softmax_lse=True, **kw)
+    stream = torch.cuda.current_stream(dev)
 
     def barrier():
         if ws > 1:
@@ -318,103 +538,59 @@ def run_gpu(args):
             dist.barrier()
         torch.cuda.synchronize()
 
-    for _ in range(args.warmup):
-        step()
+    if q is not None:
+        for _ in range(args.warmup):
+            A.sparse_attn_sharedkv(q, return_softmax_lse=True, **kw)
     barrier()
-    info = A.last_plan_info
-    launches_per_step = 1 + (1 if info.num_split_rows > 0 else 0)
+    info = A.last_plan_info if q is not None else None
+    launches_per_step = (0 if info is None else 1 + (1 if info.num_split_rows > 0 else 0))
 
-    # ---- value: K steps, device time (per-step events when L2 is flushed) ----
-    stream = torch.cuda.current_stream(dev)
+    # ---- value: K full calls, device time per step (max over ranks) ----
     sampler = ClockSampler(local)
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)]
     barrier()
-    with sampler:
-        for i in range(args.steps):
-            if flush is not None:
-                flush.zero_()
-            evs[i][0].record(stream)
-            step()
-            evs[i][1].record(stream)
-        barrier()
-    step_ms = [a.elapsed_time(b) for a, b in evs]
+    if q is not None:
+        step_ms = step_times_ms(A, q, kw, args.steps, flush, stream, sampler)
+    else:
+        with sampler:
+            pass
+        step_ms = [0.0] * args.steps
+    barrier()
     total_ms = sum(step_ms)
 
     # ---- roofline: the attention kernel alone (same plan, same inputs) ----
-    import ctypes as C
+    kern_ms = kernel_alone_ms(A, q, kw, args.steps, flush, stream) if q is not None else 0.0
 
-    from sparse_attn_sharedkv_b200 import _lib
-    key_ws = None
-    for k, v in A._PLAN_CACHE.items():
-        key_ws = v
-    ws_t, nbytes, pinfo = key_ws
-    prob, fp, keep = _rebuild_call(A, case, kw)
-    L = _lib.lib()
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)]
-    for i in range(args.steps):
-        if flush is not None:
-            flush.zero_()
-        kev[i][0].record(stream)
-        _lib.check("sas_fwd_execute",
-                   L.sas_fwd_execute(C.byref(prob), C.byref(fp), C.byref(pinfo), ws_t.data_ptr(),
-                                     nbytes, C.c_void_p(stream.cuda_stream), _lib.PHASE_ATTN))
-        kev[i][1].record(stream)
-    torch.cuda.synchronize()
-    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
-
-    # ---- e2e: host buffers in, LSE out, through the public API ----
-    host = {"q": q.cpu().pin_memory()}
-    dev_bufs = {"q": torch.empty_like(q)}
-    for name in ("cmp_sparse_indices", "ori_block_table", "cmp_block_table"):
-        t = kw.get(name)
-        if isinstance(t, torch.Tensor) and t.is_cuda:
-            host[name] = t.cpu().pin_memory()
-            dev_bufs[name] = torch.empty_like(t)
-    h2d = sum(t.numel() * t.element_size() for t in host.values())
-    lse_host = None
+    # ---- e2e: host buffers in and out, through the public API ----
     e2e_steps = max(1, min(args.steps, 20))
     barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(e2e_steps):
-        for name, t in host.items():
-            dev_bufs[name].copy_(t, non_blocking=True)
-        kw2 = dict(kw)
-        for name in dev_bufs:
-            if name != "q":
-                kw2[name] = dev_bufs[name]
-        out, lse = A.sparse_attn_sharedkv(dev_bufs["q"], return_softmax_lse=True, **kw2)
-        if lse_host is None:
-            lse_host = torch.empty(lse.shape, dtype=lse.dtype, pin_memory=True)
-        lse_host.copy_(lse, non_blocking=True)
-    e1.record(stream)
+    if q is not None:
+        e2e_ms, h2d, d2h = e2e_pipelined(A, q, kw, e2e_steps, dev)
+    else:
+        e2e_ms, h2d, d2h = 0.0, 0, 0
     barrier()
-    e2e_ms = e0.elapsed_time(e1) / e2e_steps
-    d2h = lse_host.numel() * lse_host.element_size()
 
-    # ---- N > 1: the one exchange of a sharded call, an all-gather of the
-    # output / LSE shards over NCCL (timed apart from `value`) ----
-    gather_ms, gather_bytes, gather_note = 0.0, 0, None
+    # ---- N > 1: the sharded call's one exchange, a gather of the output /
+    # LSE shards to rank 0 over NCCL (timed apart from value and e2e) ----
+    gather_ms, gather_bytes = 0.0, 0
     if ws > 1:
-        from sparse_attn_sharedkv_b200 import sharding as SH
-        out_t, lse_t = A.sparse_attn_sharedkv(q, return_softmax_lse=True, **kw)
-        n_units = out_t.shape[0]
-        gather_bytes = ws * (out_t.numel() * out_t.element_size() + lse_t.numel() * 4)
-        if gather_bytes <= (16 << 30):
-            plan = [(r * n_units, (r + 1) * n_units) for r in range(ws)]
-            args_g = (plan, rank, tuple(out_t.shape[1:]), tuple(lse_t.shape[1:]), out_t.dtype, dev)
-            SH.gather_outputs(out_t, lse_t, *args_g)  # warm-up
-            barrier()
-            g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            g0.record(stream)
-            SH.gather_outputs(out_t, lse_t, *args_g)
-            g1.record(stream)
-            barrier()
-            gather_ms = g0.elapsed_time(g1)
+        o_shape = (full.q.shape[-2], full.head_dim_v or full.q.shape[-1])
+        unit_o = o_shape if full.layout_q == "TND" else (full.q.shape[1],) + o_shape
+        unit_l = o_shape[:1] if full.layout_q == "TND" else (full.q.shape[1], o_shape[0])
+        if q is not None:
+            out_t, lse_t = A.sparse_attn_sharedkv(q, return_softmax_lse=True, **kw)
         else:
-            gather_note = "skipped: gathered output above 16 GB per rank"
+            out_t = lse_t = None
+        gargs = (bounds, rank, unit_o, unit_l, full.q.dtype, dev)
+        SH.gather_to_rank0(out_t, lse_t, *gargs)  # warm-up
+        barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        SH.gather_to_rank0(out_t, lse_t, *gargs)
+        g1.record(stream)
+        barrier()
+        gather_ms = g0.elapsed_time(g1)
+        gather_bytes = (acct_full["tokens"] if full.layout_q == "TND" else full.q.shape[0]
+                        * full.q.shape[1]) * o_shape[0] * (o_shape[1] * full.q.element_size() + 4)
         del out_t, lse_t
 
     # ---- max over ranks ----
@@ -423,69 +599,84 @@ def run_gpu(args):
         import torch.distributed as dist
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
     total_ms, kern_ms, e2e_ms, gather_ms = vals.tolist()
+    clocks = sampler.summary()
+    peaks, peak_src = load_peaks()
 
-    if rank == 0:
-        peaks, peak_src = load_peaks()
-        flops, nbytes_alg = acct["flops"], acct["bytes"]
-        ms_step = total_ms / args.steps
-        value = ws * flops * args.steps / (total_ms * 1e-3) / 1e12
-        ridge = peaks["bf16_tflops"] * 1e12 / (peaks["hbm_gbs"] * 1e9)
-        bound = "hbm" if flops / nbytes_alg < ridge else "tensor"
-        if bound == "hbm":
-            ach = nbytes_alg / (kern_ms * 1e-3) / 1e9
-            peak = peaks["hbm_gbs"]
-            unit = "GB/s"
-        else:
-            ach = flops / (kern_ms * 1e-3) / 1e12
-            peak = peaks["bf16_tflops"]
-            unit = "TFLOP/s"
-        # CPU baseline on this host (rank 0, N=1 only).
-        cpu = None
-        if ws == 1 and not args.no_cpu_baseline:
-            c_cpu = case.to("cpu")
+    # ---- N = 1: the other configurations, and the CPU baseline ----
+    per_config, cpu = None, None
+    if ws == 1:
+        c_cpu = None
+        if not args.no_cpu_baseline:
+            c_cpu = full.to("cpu")
+        del q, kw, full, kw_full, flush
+        A._PLAN_CACHE.clear()
+        gc.collect()
+        torch.cuda.empty_cache()
+        if not args.no_per_config:
+            per_config = other_configs(A, W, [c for c in range(5) if c != cfg], dev, stream,
+                                       peaks, min(args.steps, 20))
+        if c_cpu is not None:
             ftok = per_token_flops(c_cpu)
             f, s, t, threads = cpu_sample_run(c_cpu, lambda o: ftok[o], args.cpu_seconds)
-            cpu = {"value": f / s / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                   "sample": f"{t} of {acct['tokens']} query tokens (random), {s:.1f} s"}
-        clocks = sampler.summary()
+            _, host = cpu_threads()
+            cpu = {"value": f / s / 1e12, "unit": "TFLOP/s", "cores": threads,
+                   "host_cores": host, "kind": "port",
+                   "sample": f"{t} of {acct_full['tokens']} query tokens (random), {s:.1f} s, "
+                             f"{threads} BLAS threads on a {host}-core host"}
+
+    if rank == 0:
+        flops = acct_full["flops"]
+        ms_step = total_ms / args.steps
+        value = flops * args.steps / (total_ms * 1e-3) / 1e12
+        bound, ach, peak, unit = roofline(acct, kern_ms, peaks)
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if ws > 1 else "weak",
+            "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic (seeded N(0,1)*0.5, random block tables)",
             "config": {
-                "workload": W.BASELINE_NAMES[cfg], "tokens": acct["tokens"],
-                "keys": acct["keys"], "flops_per_step": flops, "bytes_per_step": nbytes_alg,
+                "workload": W.BASELINE_NAMES[cfg], "tokens": acct_full["tokens"],
+                "keys": acct_full["keys"], "flops_per_step": flops,
+                "bytes_per_step": acct_full["bytes"],
                 "us_per_call": ms_step * 1e3,
-                "hbm_gbs_per_gpu": nbytes_alg / (ms_step * 1e-3) / 1e9,
+                "hbm_gbs_per_gpu": acct_full["bytes"] / ws / (ms_step * 1e-3) / 1e9,
                 "l2": ("flushed between steps (256 MB write)" if in_l2
                        else "inputs larger than L2 (126 MB)"),
-                "parallelism": (f"dp{ws}: one shard (a copy of the configuration's sequences) "
-                                f"per rank, weak scaling"),
-                "plan": {"workers": info.num_workers, "head_groups": info.head_groups,
-                         "split_rows": info.num_split_rows, "tiles": int(info.total_tiles)},
+                "parallelism": ("single GPU" if ws == 1 else
+                                f"{ws} ranks: the call's rows split "
+                                f"{'by batch' if full.layout_q != 'TND' else 'by token ranges'}"
+                                f" (sharding.plan_shards), strong scaling"),
+                "plan": (None if info is None else
+                         {"workers": info.num_workers, "head_groups": info.head_groups,
+                          "split_rows": info.num_split_rows, "tiles": int(info.total_tiles)}),
             },
-            "e2e": {"value": ws * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "e2e": {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": e2e_ms},
+                    "ms_per_step": e2e_ms,
+                    "what": "public API per step: inputs (q, indices, block tables) copied "
+                            "from pinned host memory, output and LSE copied back to pinned "
+                            "host memory; steps pipelined over three streams"
+                            + ("; each rank copies its own shard" if ws > 1 else "")},
             "roofline": {"bound": bound, "achieved": ach, "peak": peak, "unit": unit,
                          "frac": ach / peak, "peak_source": f"{peak_src} (burst)",
                          "kernel": "sas_fwd_kernel", "kernel_ms": kern_ms,
-                         "algorithmic_bytes": nbytes_alg, "algorithmic_flops": flops,
-                         "traffic": load_traffic(W.BASELINE_NAMES[cfg]),
-                         "tensor_tflops": flops / (kern_ms * 1e-3) / 1e12,
-                         "hbm_gbs": nbytes_alg / (kern_ms * 1e-3) / 1e9},
+                         "algorithmic_bytes": acct["bytes"], "algorithmic_flops": acct["flops"],
+                         "traffic": load_traffic(W.BASELINE_NAMES[cfg]) if ws == 1 else None,
+                         "tensor_tflops": acct["flops"] / (kern_ms * 1e-3) / 1e12,
+                         "hbm_gbs": acct["bytes"] / (kern_ms * 1e-3) / 1e9},
             "cpu_baseline": cpu,
-            "allgather": (None if ws == 1 else
-                          {"ms": gather_ms, "bytes_gathered_per_rank": gather_bytes,
-                           "what": "NCCL all-gather of every rank's output and LSE shard "
-                                   "(the sharded call's one exchange); not part of value",
-                           "note": gather_note}),
+            "per_config": per_config,
+            "gather": (None if ws == 1 else
+                       {"ms": gather_ms, "bytes": gather_bytes,
+                        "what": "NCCL gather of every rank's output / LSE shard to rank 0 "
+                                "(the sharded call's one exchange); not part of value or e2e"}),
             "clocks": clocks,
             "gpu_launches": launches_per_step * args.steps,
         }
         if args.comparator == "flashmla":
-            line["comparator"] = flashmla_comparator(A, case, kw)
+            c2 = W.baseline_case(cfg, device=dev)
+            line["comparator"] = flashmla_comparator(A, c2, host_lengths(c2.kwargs()))
         print(json.dumps(line), flush=True)
     if ws > 1:
         import torch.distributed as dist
@@ -545,8 +736,8 @@ def flashmla_comparator(A, case, kw, reps: int = 20):
             "kernel_ms": times[len(times) // 2], "max_abs_diff_out": diff}
 
 
-def _rebuild_call(A, case, kw):
-    """Argument structs of the last call (to launch the attention kernel
+def _rebuild_call(A, q, kw):
+    """Argument structs of one call of (q, kw) (to launch the attention kernel
     alone through sas_fwd_execute on the cached plan)."""
     import ctypes as C
 
@@ -566,7 +757,7 @@ def _rebuild_call(A, case, kw):
     L.sas_fwd_execute = Capture()
     try:
         # The returned (out, lse) own the memory fp.out / fp.lse point to: keep them.
-        keep = A.sparse_attn_sharedkv(case.q, return_softmax_lse=True, **kw)
+        keep = A.sparse_attn_sharedkv(q, return_softmax_lse=True, **kw)
     finally:
         L.sas_fwd_execute = orig_exec
     torch.cuda.synchronize()
@@ -578,11 +769,14 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5],
-                    help="benchmark configuration (1-based); default 2 (SWA prefill)")
+    ap.add_argument("--config", type=int, default=4, choices=[1, 2, 3, 4, 5],
+                    help="benchmark configuration (1-based); default 4 (sparse prefill, "
+                         "T=32768, H=128, top-k 2048: the largest single-GPU configuration)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-per-config", action="store_true",
+                    help="skip the per-configuration times of the other four workloads")
     ap.add_argument("--comparator", default=None, choices=["flashmla"],
                     help="also time vLLM's FlashMLA sparse kernel on the same inputs "
                          "(configs 3 and 4; informational, not part of value)")

@@ -239,3 +239,33 @@ def gather_outputs(out: Optional[torch.Tensor], lse: Optional[torch.Tensor],
     dist.all_gather(gl, pad_l, group=group)
     return (torch.cat([go[r][:sizes[r]] for r in range(world)], 0),
             torch.cat([gl[r][:sizes[r]] for r in range(world)], 0))
+
+
+def gather_to_rank0(out: Optional[torch.Tensor], lse: Optional[torch.Tensor],
+                    plan: List[Tuple[int, int]], rank: int, unit_shape: Tuple[int, ...],
+                    lse_unit_shape: Tuple[int, ...], dtype: torch.dtype, device,
+                    group=None) -> Optional[Tuple[torch.Tensor, torch.Tensor]]:
+    """Gather the output / LSE shards into the full call's tensors on rank 0
+    only (the rank that needs the whole output); other ranks send and get
+    None.  Moves one copy of the output across the links instead of the N
+    copies an all-gather makes.  Shards are padded to the largest one (every
+    rank takes the same collective steps)."""
+    import torch.distributed as dist
+
+    world = len(plan)
+    sizes = [e - b for b, e in plan]
+    mx = max(max(sizes), 1)
+    pad_o = torch.zeros((mx, *unit_shape), dtype=dtype, device=device)
+    pad_l = torch.zeros((mx, *lse_unit_shape), dtype=torch.float32, device=device)
+    n = sizes[rank]
+    if n:
+        pad_o[:n].copy_(out.reshape(n, *unit_shape))
+        pad_l[:n].copy_(lse.reshape(n, *lse_unit_shape))
+    go = [torch.empty_like(pad_o) for _ in range(world)] if rank == 0 else None
+    gl = [torch.empty_like(pad_l) for _ in range(world)] if rank == 0 else None
+    dist.gather(pad_o, go, dst=0, group=group)
+    dist.gather(pad_l, gl, dst=0, group=group)
+    if rank != 0:
+        return None
+    return (torch.cat([go[r][:sizes[r]] for r in range(world)], 0),
+            torch.cat([gl[r][:sizes[r]] for r in range(world)], 0))

@@ -2,7 +2,7 @@
 
 The fixtures (``tests/golden/attn_golden.*``) hold the reference golden's
 outputs; the inputs are regenerated from the recorded parameters by
-``sparse_attn_sharedkv_b200.workloads`` (same seeds, same RNG call order).
+``tests.workloads`` (same seeds, same RNG call order).
 """
 
 from __future__ import annotations
@@ -14,7 +14,7 @@ from typing import Dict, Tuple
 import numpy as np
 import torch
 
-from sparse_attn_sharedkv_b200 import workloads as W
+from tests import workloads as W
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 GOLDEN_DIR = os.path.join(HERE, "golden")

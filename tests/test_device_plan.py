@@ -10,7 +10,7 @@ import pytest
 import torch
 
 from sparse_attn_sharedkv_b200 import _lib
-from sparse_attn_sharedkv_b200 import workloads as W
+from tests import workloads as W
 from sparse_attn_sharedkv_b200.api import build_call, sparse_attn_sharedkv
 
 pytestmark = pytest.mark.gpu
@@ -74,6 +74,13 @@ CASES = [
           kv_lens=(9000, 40, 7000, 64, 128, 3000), K=2048, ratio=1, win_left=-1, scenario=3), 296),
     (dict(seed=307, layout_q="TND", B=1, H=64, q_lens=(1,), kv_lens=(100,), K=64,
           scenario=3), 1),
+    # rows of 4 tiles (kept whole) and 5 tiles (cut) next to worker boundaries
+    (dict(seed=308, layout_q="BSND", B=12, H=64, q_lens=(1,) * 12,
+          kv_lens=(256, 257, 256, 320, 193, 257, 256, 300, 256, 256, 257, 320), K=512,
+          ratio=1, win_left=-1, scenario=3), 7),
+    (dict(seed=308, layout_q="BSND", B=12, H=64, q_lens=(1,) * 12,
+          kv_lens=(256, 257, 256, 320, 193, 257, 256, 300, 256, 256, 257, 320), K=512,
+          ratio=1, win_left=-1, scenario=3), 11),
 ]
 
 

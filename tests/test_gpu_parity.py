@@ -21,7 +21,7 @@ import torch
 os.environ.setdefault("SAS_CHECK_DEVICE_ERRORS", "1")
 
 from oracle import sas_oracle as O  # noqa: E402
-from sparse_attn_sharedkv_b200 import workloads as W  # noqa: E402
+from tests import workloads as W  # noqa: E402
 from sparse_attn_sharedkv_b200.api import sparse_attn_sharedkv  # noqa: E402
 from sparse_attn_sharedkv_b200.sparse_flash_mla_api import sparse_flash_mla  # noqa: E402
 from tests.checks import (check_lse_tight, check_north_star, check_reference_lse,  # noqa: E402
@@ -67,6 +67,8 @@ def test_golden_vectors(key):
     toks = meta["tokens"]
     if toks is not None:
         out, lse = out[toks], lse[toks]
+    if meta.get("heads") is not None:
+        out = out[:, meta["heads"]]
     if meta["kind"] == "reference_scenario":
         check_reference_result(out, exp_out, meta["dtype"])
         check_reference_lse(lse, exp_lse, meta["dtype"])
@@ -83,20 +85,73 @@ def test_golden_vectors(key):
         print(key, check_north_star(out, ref, gold))
 
 
-@pytest.mark.parametrize("cfg", range(5))
-def test_baseline_workloads_full_size(cfg):
-    case = W.baseline_case(cfg, device=DEV)
+def split_row_tokens(case: W.Case):
+    """Flat tokens of the rows that the host planner (this GPU's SM count, the
+    plan the call runs) splits across workers: the rows whose pieces go
+    through the fp32 partials and the combine kernel."""
+    from sparse_attn_sharedkv_b200.api import build_call
+    from tests.test_plan import build_plan
+    call = build_call(case.q, **case.kwargs())
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    plan, info = build_plan(call.prob, sms)
+    off = int(info.split_off)
+    return [int(plan[off + 4 * i]) for i in range(info.num_split_rows)]
+
+
+def record_stats(name, stats, **extra):
+    """Append the parity statistics of a full-size case to the JSON-lines file
+    named by SAS_PARITY_STATS (if set), for the committed record."""
+    path = os.environ.get("SAS_PARITY_STATS")
+    if path:
+        import json
+        with open(path, "a") as f:
+            f.write(json.dumps(dict(case=name, **stats, **extra)) + "\n")
+
+
+def check_full_size(case, name, toks):
     out, lse = run(case)
     c = case.to("cpu")
-    T = c.q.shape[0] * (c.q.shape[1] if c.layout_q == "BSND" else 1)
-    rng = np.random.default_rng(cfg)
-    toks = sorted(set([0, T - 1] + rng.choice(T, size=min(T, 24), replace=False).tolist()))
     ex, gold, o_lse = oracle(c, tokens=toks)
     fo, fl = flat_tokens(out, c.layout_q), flat_tokens(lse, c.layout_q)
     ro, rg, rl = (flat_tokens(a, c.layout_q) for a in (ex, gold, o_lse))
     stats = check_north_star(fo[toks], ro[toks], rg[toks])
     check_lse_tight(fl[toks], rl[toks])
-    print(f"cfg{cfg + 1}: {stats}")
+    print(f"{name}: {stats} on {len(toks)} tokens")
+    return stats
+
+
+@pytest.mark.parametrize("cfg", range(5))
+def test_baseline_workloads_full_size(cfg):
+    """Full-size benchmark workloads: every token of the decode batches of up
+    to 64 rows, and for the larger ones every row the plan splits across
+    workers (with its neighbours) plus the first, last and 24 random tokens."""
+    case = W.baseline_case(cfg, device=DEV)
+    T = case.q.shape[0] * (case.q.shape[1] if case.layout_q == "BSND" else 1)
+    split = split_row_tokens(case)
+    if T <= 64:
+        toks = list(range(T))
+    else:
+        rng = np.random.default_rng(cfg)
+        pick = {0, T - 1, *rng.choice(T, size=min(T, 24), replace=False).tolist()}
+        for t in split:
+            pick.update(x for x in (t - 1, t, t + 1) if 0 <= x < T)
+        toks = sorted(pick)
+    stats = check_full_size(case, f"cfg{cfg + 1}", toks)
+    record_stats(W.BASELINE_NAMES[cfg], stats, tokens_checked=len(toks),
+                 split_rows=len(split), total_tokens=T)
+
+
+def test_cfg3_minus_one_padding_full_size():
+    """cfg3 with half the sequences shorter than top-k 2048, so their index
+    rows end in -1 padding (golden.py:48-62): every row checked."""
+    case = W.baseline_case(2, device=DEV, minus_one_variant=True)
+    idx = case.cmp_sparse_indices.reshape(case.q.shape[0], -1)
+    padded = int((idx == -1).any(dim=1).sum())
+    assert padded >= case.q.shape[0] // 2 - 1
+    T = case.q.shape[0]
+    stats = check_full_size(case, "cfg3_minus_one", list(range(T)))
+    record_stats("cfg3_minus_one_variant", stats, tokens_checked=T, padded_rows=padded,
+                 split_rows=len(split_row_tokens(case)), total_tokens=T)
 
 
 @pytest.mark.parametrize("num_sms", [1, 5, 37, 148, 296])

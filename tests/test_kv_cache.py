@@ -94,7 +94,7 @@ def test_gpu_append_reports_unmapped_page():
 def test_appended_cache_feeds_attention():
     # Build a cache by appending, then run the forward: equal to the forward on
     # the directly generated cache (the writer produces the path's input layout).
-    from sparse_attn_sharedkv_b200 import workloads as W
+    from tests import workloads as W
     from sparse_attn_sharedkv_b200.api import sparse_attn_sharedkv
     from sparse_attn_sharedkv_b200.kv_cache import append_paged_kv
     case = W.random_case(seed=91, layout_q="TND", H=64, q_lens=(3, 2), kv_lens=(700, 300),

@@ -14,7 +14,7 @@ import os
 import pytest
 import torch
 
-from sparse_attn_sharedkv_b200 import workloads as W
+from tests import workloads as W
 from sparse_attn_sharedkv_b200.metadata import (AIC_CORE_NUM, FA_METADATA_SIZE, SAS_META_SIZE,
                                                 sparse_attn_sharedkv_metadata)
 

@@ -16,7 +16,7 @@ import torch
 
 from oracle import sas_oracle as O
 from sparse_attn_sharedkv_b200 import _lib
-from sparse_attn_sharedkv_b200 import workloads as W
+from tests import workloads as W
 
 HDR = dict(magic=0, rows=1, workers=2, hg=3, nsplit=4, npart=5, rows_off=6, workers_off=7,
            split_off=8, total=9, batch=10, actq_off=11, actkv_off=12)
@@ -242,6 +242,51 @@ def test_kernel_slot_logic_matches_oracle(kw, sms):
             assert sorted(got.get(r, [])) == sorted(exp), (r, t)
         else:
             assert got.get(r, []) == exp, (r, t)
+
+
+# Decode rows of exactly 4 key tiles (256 keys: kept whole) and 5 tiles
+# (257..320 keys: cut at tile granularity) side by side.
+SNAP_KV = [256, 257, 256, 320, 193, 257, 256, 300, 256, 256, 257, 320]
+
+
+def _snap_problem():
+    B = len(SNAP_KV)
+    return make_problem("BSND", list(range(B)), [1] * B, SNAP_KV, 64, 3, -1, 1, 512, 1)
+
+
+@pytest.mark.parametrize("sms", range(2, 30))
+def test_short_rows_whole_next_to_worker_boundaries(sms):
+    p, keep = _snap_problem()
+    plan, info = build_plan(p, sms)
+    rows = rows_of(plan)
+    owners = {}
+    for w, r, ja, jb, piece in segments(plan):
+        owners.setdefault(r, []).append(w)
+    for r, row in enumerate(rows):
+        if (row[3] + 63) // 64 <= 4:
+            assert len(owners[r]) == 1, (sms, r)
+
+
+def test_snap_sweep_exercises_both_sides_of_the_rule():
+    """Across the worker counts above, some worker boundary falls inside a
+    4-tile row (kept whole) and some 5-tile row is split (cut as usual)."""
+    p, keep = _snap_problem()
+    cut4 = split5 = False
+    for sms in range(2, 30):
+        plan, info = build_plan(p, sms)
+        starts = np.cumsum([0] + [1 + (k + 63) // 64 for k in SNAP_KV])
+        total = starts[-1]
+        bounds = [total * w / sms for w in range(1, sms)]
+        for r, k in enumerate(SNAP_KV):
+            tiles = (k + 63) // 64
+            inside = any(starts[r] < x < starts[r + 1] for x in bounds)
+            if tiles == 4 and inside:
+                cut4 = True
+        owners = {}
+        for w, r, ja, jb, piece in segments(plan):
+            owners.setdefault(r, []).append(w)
+        split5 |= any(len(v) > 1 and (SNAP_KV[r] + 63) // 64 == 5 for r, v in owners.items())
+    assert cut4 and split5
 
 
 def test_plan_rejects_bad_problems():

@@ -16,7 +16,7 @@ import torch
 
 os.environ.setdefault("SAS_CHECK_DEVICE_ERRORS", "1")
 
-from sparse_attn_sharedkv_b200 import workloads as W  # noqa: E402
+from tests import workloads as W  # noqa: E402
 from tests.checks import check_lse_tight, check_north_star  # noqa: E402
 from tests.test_gpu_parity import oracle, run  # noqa: E402
 

@@ -14,7 +14,7 @@ import torch.multiprocessing as mp
 
 from oracle import sas_oracle as O
 from sparse_attn_sharedkv_b200 import sharding as SH
-from sparse_attn_sharedkv_b200 import workloads as W
+from tests import workloads as W
 from tests.golden_cases import case_to_numpy
 
 CASES = [
@@ -95,7 +95,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _gloo_worker(rank, world, port, i, result_dir):
+def _gloo_worker(rank, world, port, i, result_dir, mode="all"):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -114,7 +114,12 @@ def _gloo_worker(rank, world, port, i, result_dir):
         if not sh.empty:
             o, l = _oracle(sh.q, sh.kwargs)
             o, l = torch.from_numpy(o), torch.from_numpy(l)
-        go, gl = SH.gather_outputs(o, l, plan, rank, unit, lunit, torch.float32, "cpu")
+        if mode == "all":
+            go, gl = SH.gather_outputs(o, l, plan, rank, unit, lunit, torch.float32, "cpu")
+        else:
+            res = SH.gather_to_rank0(o, l, plan, rank, unit, lunit, torch.float32, "cpu")
+            assert (res is None) == (rank != 0)
+            go, gl = res if res is not None else (None, None)
         if rank == 0:
             np.save(os.path.join(result_dir, "out.npy"), go.numpy())
             np.save(os.path.join(result_dir, "lse.npy"), gl.numpy())
@@ -127,6 +132,17 @@ def test_two_rank_gloo_allgather(i, tmp_path):
     world = 2
     mp.start_processes(_gloo_worker, args=(world, _free_port(), i, str(tmp_path)), nprocs=world,
                        join=True, start_method="spawn")
+    c = _case(i)
+    full_out, full_lse = _oracle(c.q, c.kwargs())
+    assert np.array_equal(np.load(tmp_path / "out.npy").reshape(full_out.shape), full_out)
+    assert np.array_equal(np.load(tmp_path / "lse.npy").reshape(full_lse.shape), full_lse)
+
+
+@pytest.mark.parametrize("i", [0, 4])
+def test_two_rank_gloo_gather_to_rank0(i, tmp_path):
+    world = 2
+    mp.start_processes(_gloo_worker, args=(world, _free_port(), i, str(tmp_path), "rank0"),
+                       nprocs=world, join=True, start_method="spawn")
     c = _case(i)
     full_out, full_lse = _oracle(c.q, c.kwargs())
     assert np.array_equal(np.load(tmp_path / "out.npy").reshape(full_out.shape), full_out)

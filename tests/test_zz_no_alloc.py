@@ -24,7 +24,7 @@ import pytest
 import torch
 
 from sparse_attn_sharedkv_b200 import _lib
-from sparse_attn_sharedkv_b200 import workloads as W
+from tests import workloads as W
 from sparse_attn_sharedkv_b200.api import build_call
 
 pytestmark = pytest.mark.gpu

@@ -312,6 +312,17 @@ REFERENCE_SCENARIOS = {
     "cfa_decode": dict(_REF_COMMON, scenario=2, S1=1, T1=1, K=512, block_num1=65,
                        block_num2=17, block_size1=128, block_size2=128,
                        cu_seqlens_q=[0, 1], seqused_kv=[8193], cmp_ratio=128),
+    # Full-length prefills (S1 = 8192), test_sparse_attn_sharedkv.py:105-128,
+    # 151-174, 197-220.
+    "scfa_prefill": dict(_REF_COMMON, scenario=3, S1=8192, T1=8192, K=512, block_num1=65,
+                         block_num2=17, block_size1=128, block_size2=128,
+                         cu_seqlens_q=[0, 8192], seqused_kv=[8192], cmp_ratio=4),
+    "swa_prefill": dict(_REF_COMMON, scenario=1, S1=8192, T1=8192, K=0, block_num1=65,
+                        block_num2=1, block_size1=128, block_size2=1,
+                        cu_seqlens_q=[0, 8192], seqused_kv=[8192], cmp_ratio=4),
+    "cfa_prefill": dict(_REF_COMMON, scenario=2, S1=8192, T1=8192, K=512, block_num1=65,
+                        block_num2=17, block_size1=128, block_size2=128,
+                        cu_seqlens_q=[0, 8192], seqused_kv=[8192], cmp_ratio=128),
 }
 
 
