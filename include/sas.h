@@ -136,6 +136,18 @@ typedef struct SasFwdParams {
   int32_t num_sms;                 /* persistent workers (0 = all SMs)            */
   int64_t* trace;                  /* [device] optional int64[4 * 8192] clock trace
                                       of CTA 0 (diagnostics; NULL = off)           */
+  int32_t* slot_dump;              /* [device] optional int32[total_tokens,
+                                      slot_dump_cap]: the key source each slot of a
+                                      query row resolved to (diagnostics; NULL =
+                                      off): 2 * pool_row + cache (0 window, 1
+                                      compressed), -2 - cache for an attended
+                                      position whose page is unmapped (zero row),
+                                      -1 for a masked slot; entries not written are
+                                      left as they are.  Slot order is window keys
+                                      then compressed keys (golden.py tile order);
+                                      a ring row (one head group, a 65..128-key
+                                      window) uses its ring order instead.        */
+  int32_t slot_dump_cap;           /* row stride of slot_dump (slots per token)    */
 } SasFwdParams;
 
 /* Plan summary returned by sas_plan (sizes in elements). */

@@ -71,6 +71,7 @@ class SasFwdParams(C.Structure):
         ("cmp_block_size", C.c_int32), ("cmp_num_blocks", C.c_int32),
         ("cmp_table_len", C.c_int32),
         ("num_sms", C.c_int32), ("trace", C.c_void_p),
+        ("slot_dump", C.c_void_p), ("slot_dump_cap", C.c_int32),
     ]
 
 

@@ -19,7 +19,7 @@ LIB_DIR = os.path.join(PKG, "_lib")
 LIB = os.path.join(LIB_DIR, "libsas.so")
 INCLUDE = os.path.join(REPO, "include")
 
-SOURCES = ["sas_capi.cu", "sas_fwd.cu", "sas_combine.cu", "sas_noalloc.cu", "sas_kvwrite.cu",
+SOURCES = ["sas_capi.cu", "sas_fwd.cu", "sas_fwd_pair.cu", "sas_combine.cu", "sas_noalloc.cu", "sas_kvwrite.cu",
            "sas_plan_dev.cu", "sas_plan.cpp", "sas_metadata.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

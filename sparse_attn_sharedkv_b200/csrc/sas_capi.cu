@@ -207,9 +207,19 @@ extern "C" int sas_fwd_execute(const SasProblem* prob, const SasFwdParams* param
     const char* e = getenv("SAS_GATHER");
     a.gather = (e != nullptr && strcmp(e, "lsu") == 0) ? 0 : 1;
   }
+  a.slot_dump = f.slot_dump;
+  a.slot_dump_cap = f.slot_dump != nullptr ? f.slot_dump_cap : 0;
   int rc = SAS_OK;
   if (phases & SAS_PHASE_ATTN) {
-    rc = sas::launch_fwd(a, info.num_workers * info.head_groups, stream);
+    // Two head groups (65..128 heads) run on one CTA per head group, or on
+    // CTA pairs issuing cta_group::2 MMAs when SAS_FWD_KERNEL=pair (read at
+    // each call).
+    const char* ek = getenv("SAS_FWD_KERNEL");
+    const bool pair = ek != nullptr && strcmp(ek, "pair") == 0;
+    if (info.head_groups == 2 && pair)
+      rc = sas::launch_fwd_pair(a, info.num_workers, stream);
+    else
+      rc = sas::launch_fwd(a, info.num_workers * info.head_groups, stream);
     if (rc != SAS_OK) return rc;
   }
   if ((phases & SAS_PHASE_COMBINE) && info.num_split_rows > 0) {

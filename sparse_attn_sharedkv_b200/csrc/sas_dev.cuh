@@ -405,6 +405,16 @@ __device__ __forceinline__ SlotSrc resolve_slot(const FwdArgs& a, const Row& rv,
 }
 
 
+// Diagnostic record of the key source of slot `slot` of token `token`
+// (FwdArgs::slot_dump): 2 * row + cache, -2 - cache for an attended position
+// whose page is unmapped, -1 for a masked slot.
+__device__ __forceinline__ void dump_slot(const FwdArgs& a, int token, int slot,
+                                          const SlotSrc& s) {
+  if (slot >= a.slot_dump_cap) return;
+  const int v = s.valid ? (s.row >= 0 ? s.row * 2 + s.pool : -2 - s.pool) : -1;
+  a.slot_dump[(size_t)token * a.slot_dump_cap + slot] = v;
+}
+
 // Coalesced store of one warp's 32 rows x 32 bytes: lane i holds row i's
 // 32 bytes in v[0..1].  The rows go through the warp's 1 KB staging buffer
 // (16-byte slot q of row i at slot q ^ ((i >> 2) & 1): conflict-free both

@@ -545,6 +545,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int half = stage ^ ring_sigma;
           const SlotSrc sa = resolve_ring(args, rv, half, pw * 16 + (lane & 15), err);
           const uint32_t va_cur = __ballot_sync(0xffffffffu, sa.valid);
+          if (args.slot_dump != nullptr && lane < 16)
+            dump_slot(args, rv.token, half * kTileKeys + pw * 16 + lane, sa);
           if (leader && lane == 0) trace(tr, 0, 3 * produced);
           if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.kv_empty[stage],
                                                 (kv_empty_par >> stage) & 1u, err, 2))) {
@@ -631,6 +633,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = ja; j < jb; ++j) {
         const SlotSrc sa = nxt;
         const uint32_t va_cur = va;
+        if (args.slot_dump != nullptr && lane < 16)
+          dump_slot(args, rv.token, j * kTileKeys + pw * 16 + lane, sa);
         if (j + 1 < jb) {
           nxt = resolve_tile(args, rv, qk, idx_row, j + 1, pw, lane, &stopped, &va, err);
           if (group == 0) prefetch_rows(args, nxt, lane, row_bytes);

@@ -116,15 +116,18 @@ SAS_HD inline int64_t unit_mid2(int64_t start, int64_t tiles, int64_t j) {
   return 2 * (start + 1 + j) + 1;
 }
 
-// Windows of 65..128 keys with no compressed branch run as ring rows.
-SAS_HD inline bool ring_window(int32_t scenario, int32_t win_left) {
-  return scenario == SAS_SCENARIO_SWA && win_left >= 64 && win_left < kRingKeys;
+// Windows of 65..128 keys with no compressed branch run as ring rows when
+// the call has one head group (at most 64 heads); the two-CTA kernel used
+// for more heads walks such windows as ordinary two-tile rows.
+SAS_HD inline bool ring_window(int32_t scenario, int32_t win_left, int32_t num_heads) {
+  return scenario == SAS_SCENARIO_SWA && win_left >= 64 && win_left < kRingKeys &&
+         num_heads <= kHeadsPerCta;
 }
 
 // Key slots of a query row and its flags (both planners).
 SAS_HD inline int32_t row_slots(const QueryKeys& k, int32_t scenario, int32_t win_left,
-                                int32_t* flags) {
-  if (ring_window(scenario, win_left) && k.window > 0) {
+                                int32_t num_heads, int32_t* flags) {
+  if (ring_window(scenario, win_left, num_heads) && k.window > 0) {
     *flags = kRowRing;
     return kRingKeys;
   }

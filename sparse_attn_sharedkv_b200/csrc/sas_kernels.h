@@ -38,9 +38,12 @@ struct FwdArgs {
   int32_t ori_rows;         // ori_num_blocks * ori_block_size (out-of-range row = zero fill)
   int32_t cmp_rows;         // cmp_num_blocks * cmp_block_size
   int32_t gather;           // key-row gather: 0 = cp.async (LSU), 1 = TMA gather4 (default)
+  int32_t* slot_dump;       // optional [total_tokens, slot_dump_cap] resolved key sources
+  int32_t slot_dump_cap;
 };
 
 int launch_fwd(const FwdArgs& args, int grid, cudaStream_t stream);
+int launch_fwd_pair(const FwdArgs& args, int workers, cudaStream_t stream);
 
 int launch_combine(const int32_t* row_token, const int32_t* row_pieces, const int32_t* row_base,
                    int stride, int n, const float* o_partial, const float* lse_partial, int num_heads,

@@ -59,7 +59,7 @@ int collect_rows(const SasProblem& p, std::vector<Row>* rows) {
         sas::QueryKeys k = sas::query_keys(p.scenario, len, kv, s, p.ori_win_left, p.cmp_ratio,
                                            p.topk);
         r.window = k.window;
-        r.slots = sas::row_slots(k, p.scenario, p.ori_win_left, &r.flags);
+        r.slots = sas::row_slots(k, p.scenario, p.ori_win_left, p.num_heads, &r.flags);
         r.win_lo = k.win_lo;
         r.cmp = k.cmp;
         r.thr = k.thr;

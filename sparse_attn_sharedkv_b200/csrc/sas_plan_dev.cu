@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
       const sas::QueryKeys k = sas::query_keys(scenario, ql, kv_len[b], s, win_left, ratio, topk);
       int32_t flags = 0;
-      slots = sas::row_slots(k, scenario, win_left, &flags);
+      slots = sas::row_slots(k, scenario, win_left, hg * sas::kHeadsPerCta, &flags);
       e[sas::R_FLAGS] = flags;
       e[sas::R_WINDOW] = k.window; e[sas::R_WIN_LO] = k.win_lo;
       e[sas::R_CMP] = k.cmp; e[sas::R_THR] = k.thr;

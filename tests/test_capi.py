@@ -66,6 +66,7 @@ int main(void) {
   F(SasProblem, q_start) F(SasProblem, num_heads) F(SasProblem, topk)
   F(SasFwdParams, err) F(SasFwdParams, head_dim) F(SasFwdParams, softmax_scale)
   F(SasFwdParams, cmp_table_len) F(SasFwdParams, num_sms) F(SasFwdParams, trace)
+  F(SasFwdParams, slot_dump) F(SasFwdParams, slot_dump_cap)
   F(SasPlanInfo, total_tiles) F(SasPlanInfo, actkv_off)
   K(SAS_OK) K(SAS_ERR_INVALID) K(SAS_ERR_UNSUPPORTED) K(SAS_ERR_CUDA) K(SAS_ERR_SCHEDULE)
   K(SAS_ERR_WORKSPACE) K(SAS_ERR_DEVICE) K(SAS_DTYPE_BF16) K(SAS_DTYPE_FP16)
