@@ -511,7 +511,8 @@ def run_gpu(args):
     from tests import workloads as W
 
     cfg = args.config - 1
-    full = W.baseline_case(cfg, device=dev)
+    full = W.baseline_case(cfg, device=dev,
+                           sequences=args.sequences if cfg == 3 else None)
     acct_full = W.accounting(full)
     kw_full = host_lengths(full.kwargs())
     if ws > 1:
@@ -636,7 +637,9 @@ def run_gpu(args):
             "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic (seeded N(0,1)*0.5, random block tables)",
             "config": {
-                "workload": W.BASELINE_NAMES[cfg], "tokens": acct_full["tokens"],
+                "workload": W.BASELINE_NAMES[cfg] + ("" if args.sequences is None or cfg != 3
+                                                     else f"_seqs{args.sequences}"),
+                "tokens": acct_full["tokens"],
                 "keys": acct_full["keys"], "flops_per_step": flops,
                 "bytes_per_step": acct_full["bytes"],
                 "us_per_call": ms_step * 1e3,
@@ -775,6 +778,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sequences", type=int, default=None,
+                    help="config 4 only: keep this many of its 4096-token sequences "
+                         "(profiling captures of a few GB); default all 8")
     ap.add_argument("--no-per-config", action="store_true",
                     help="skip the per-configuration times of the other four workloads")
     ap.add_argument("--comparator", default=None, choices=["flashmla"],

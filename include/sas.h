@@ -212,6 +212,8 @@ int sas_fwd_prepare_device(const SasProblem* prob, const SasFwdParams* params, v
  * exit; a problem needing more returns SAS_ERR_WORKSPACE (fewer workers via
  * params->num_sms shrink the partials).  The array's device address is set
  * up on a device's first call: make that call before any stream capture.
+ * Each call builds its work plan on the host and copies it into the array
+ * with a stream-ordered copy from host memory before launching the kernels.
  * All calls on a device share the array (it keeps the last call's contents;
  * nothing in it needs to start at zero), so calls that overlap on the GPU
  * race: serialise them.  Makes no device allocation. */

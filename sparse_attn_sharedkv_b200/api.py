@@ -370,30 +370,43 @@ def sparse_attn_sharedkv(
 ) -> Union[torch.Tensor, Tuple[torch.Tensor, torch.Tensor]]:
     """Sparse shared-KV attention forward; see the module docstring."""
     del seqused_q, core_num  # API parity (api.py:186); the B200 plan uses all SMs
+    _check_modes(cmp_kv, ori_mask_mode, cmp_mask_mode, ori_win_right, layout_q, layout_kv)
+    if metadata is not None:
+        _require(metadata.numel() == SAS_META_SIZE,
+                 f"metadata must have {SAS_META_SIZE} int32 entries (got {metadata.numel()})")
+    out_flat, lse_flat = _checked_forward(
+        q, ori_kv=ori_kv, cmp_kv=cmp_kv, cmp_sparse_indices=cmp_sparse_indices,
+        ori_block_table=ori_block_table, cmp_block_table=cmp_block_table,
+        cu_seqlens_q=cu_seqlens_q, seqused_kv=seqused_kv, sinks=sinks,
+        softmax_scale=softmax_scale, cmp_ratio=cmp_ratio, ori_win_left=ori_win_left,
+        layout_q=layout_q, topk_cmp=topk_cmp, head_dim_v=head_dim_v, num_sms=num_sms,
+        device_plan=device_plan)
+    return _restore_layout(q, out_flat, lse_flat, layout_q, return_softmax_lse)
+
+
+def _check_modes(cmp_kv, ori_mask_mode, cmp_mask_mode, ori_win_right, layout_q, layout_kv):
+    """The mode / layout checks of both entry points (api.py:187-191)."""
     _require(ori_mask_mode == 4, "only ori_mask_mode=4 supported")
     _require(cmp_mask_mode == 3 or cmp_kv is None, "only cmp_mask_mode=3 supported")
     _require(ori_win_right == 0, "only ori_win_right=0 supported")
     _require(layout_kv == "PA_ND", "only layout_kv=PA_ND supported")
     _require(layout_q in ("TND", "BSND"), f"unsupported layout_q={layout_q!r}")
-    if metadata is not None:
-        _require(metadata.numel() == SAS_META_SIZE,
-                 f"metadata must have {SAS_META_SIZE} int32 entries (got {metadata.numel()})")
+
+
+def _checked_forward(q: torch.Tensor, **kw):
+    """_forward with the device error word when SAS_CHECK_DEVICE_ERRORS=1: a
+    device-side check that fired (an out-of-pool page id, a timed-out wait)
+    raises RuntimeError after the call."""
     err = None
     if _check_device_errors():
         err = torch.zeros(4, dtype=torch.int32, device=q.device)
-    out_flat, lse_flat = _forward(
-        q, ori_kv=ori_kv, cmp_kv=cmp_kv, cmp_sparse_indices=cmp_sparse_indices,
-        ori_block_table=ori_block_table, cmp_block_table=cmp_block_table,
-        cu_seqlens_q=cu_seqlens_q, seqused_kv=seqused_kv, sinks=sinks,
-        softmax_scale=softmax_scale, cmp_ratio=cmp_ratio, ori_win_left=ori_win_left,
-        layout_q=layout_q, topk_cmp=topk_cmp, head_dim_v=head_dim_v, num_sms=num_sms, err=err,
-        device_plan=device_plan)
+    out_flat, lse_flat = _forward(q, err=err, **kw)
     if err is not None:
         e = err.tolist()
         if e[0] != 0:
             raise RuntimeError(f"sas_fwd device check failed: code={e[0]} site={e[1]} "
                                f"detail={e[2]} block={e[3]}")
-    return _restore_layout(q, out_flat, lse_flat, layout_q, return_softmax_lse)
+    return out_flat, lse_flat
 
 
 def _restore_layout(q, out_flat, lse_flat, layout_q, return_lse):

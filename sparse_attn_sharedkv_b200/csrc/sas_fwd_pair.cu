@@ -52,7 +52,8 @@ constexpr int kPSoftmaxThreads = 128;
 constexpr int kPProducerWarp0 = 4;
 constexpr int kPMmaWarp = 8;
 constexpr int kPQWarp = 9;
-constexpr int kPMoverWarp0 = 10;  // warp 11 has no role
+constexpr int kPMoverWarp0 = 10;
+constexpr int kPPvWarp = 11;       // CTA 0: PV issuer; CTA 1: second relay thread
 constexpr int kPEpiWarp0 = 12;
 constexpr int kPEpiThreads = 128;
 constexpr int kPProducerThreads = 128;
@@ -95,8 +96,11 @@ struct PairCtl {
   uint64_t o_full, o_free, drain;
   uint64_t xbar[2];
   uint64_t fin_full[2], fin_free[2];
-  // Leader only: CTA 1's readiness, forwarded by its relay (one arrival each).
-  uint64_t m_kv_full[kNumRegions][3];
+  // Leader only: CTA 1's readiness, arrived remotely by CTA 1's roles:
+  // its rows of a region (mover, once all three chunk groups are in), its V
+  // buffer (mover), P and the S / O releases (one lane per softmax /
+  // epilogue warp), Q (Q loader).
+  uint64_t m_kv_full[kNumRegions];
   uint64_t m_vin[2], m_p_full, m_q_full, m_s_empty[2], m_o_free;
   uint32_t tmem_base;
   volatile int abort;
@@ -122,16 +126,34 @@ __device__ __forceinline__ uint32_t peer_addr(uint32_t a, uint32_t rank) {
 // A mirror barrier of the leader (arrived by CTA 1's relay), polled relaxed:
 // it only orders the leader's MMA issue after CTA 1's shared memory was
 // complete (see arrive_remote).
-__device__ __forceinline__ bool test_mirror(uint32_t bar, uint32_t parity) {
+__device__ __forceinline__ bool try_wait_mirror(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.relaxed.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.relaxed.cluster.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(bar), "r"(parity)
       : "memory");
   return ok != 0;
+}
+
+// Bounded wait on a mirror barrier; on timeout records the error and raises
+// the CTA abort flag.
+__device__ __forceinline__ bool wait_mirror(PairCtl* ctl, uint64_t* bar, uint32_t parity,
+                                            int* err, int site) {
+  const uint32_t a = smem_addr(bar);
+  if (try_wait_mirror(a, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (try_wait_mirror(a, parity)) return true;
+    if (ctl->abort) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      record_error(err, SAS_ERR_DEVICE, site, (int)parity);
+      ctl->abort = 1;
+      return false;
+    }
+  }
 }
 
 // Bulk copy of `bytes` from this CTA's shared memory to shared memory of a
@@ -438,11 +460,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         // one arrival per producer warp (lane 0, arming the TMA bytes) and
         // one cp.async completion arrival per producer lane
         mbar_init(smem_addr(&ctl.kv_full[i][g]), 4 + kPProducerThreads);
-        mbar_init(smem_addr(&ctl.m_kv_full[i][g]), 1);
       }
       // QK of the tile has read it (leader's commit) and every copy out of
       // it has landed (leader's arrival once both V buffers are complete)
       mbar_init(smem_addr(&ctl.kv_free[i]), 2);
+      mbar_init(smem_addr(&ctl.m_kv_full[i]), 1);
     }
     for (int i = 0; i < kValidRing; ++i) {
       mbar_init(smem_addr(&ctl.vfull[i]), 4);
@@ -462,14 +484,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       mbar_init(smem_addr(&ctl.xbar[i]), kPSoftmaxThreads);
       mbar_init(smem_addr(&ctl.fin_full[i]), kPSoftmaxThreads);
       mbar_init(smem_addr(&ctl.fin_free[i]), kPEpiThreads);
-      mbar_init(smem_addr(&ctl.m_s_empty[i]), 1);
+      mbar_init(smem_addr(&ctl.m_s_empty[i]), 4);
     }
     mbar_init(smem_addr(&ctl.o_full), 1);
     mbar_init(smem_addr(&ctl.o_free), kPEpiThreads);
-    mbar_init(smem_addr(&ctl.drain), 1);
-    mbar_init(smem_addr(&ctl.m_p_full), 1);
+    mbar_init(smem_addr(&ctl.drain), 2);  // one commit from each MMA issuer
+    mbar_init(smem_addr(&ctl.m_p_full), 4);
     mbar_init(smem_addr(&ctl.m_q_full), 1);
-    mbar_init(smem_addr(&ctl.m_o_free), 1);
+    mbar_init(smem_addr(&ctl.m_o_free), 4);
     ctl.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -594,6 +616,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         for (int cg = 0; cg < 3; ++cg)
           w = w && wait_bar(&ctl, &ctl.kv_full[region][cg], kpar, err, 72);
         trace(tr, 3, 4 * t + 1);
+        if (w && !leader)  // CTA 1's rows of the tile are in: tell the leader
+          arrive_remote(peer_addr(smem_addr(&ctl.m_kv_full[region]), 0u));
         if (w && t >= 2)
           w = wait_bar(&ctl, &ctl.pv_done[t & 1], (uint32_t)(((t >> 1) - 1) & 1), err, 73);
         if (!w) break;
@@ -612,6 +636,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                    peer_bar);
         }
         trace(tr, 3, 4 * t + 3);
+        const uint32_t vp = (uint32_t)((t >> 1) & 1);
+        if (leader) {
+          // Once both CTAs' V buffers hold the tile, every copy out of its
+          // gather regions has landed: release them (QK's commit is their
+          // other arrival).
+          if (!wait_bar(&ctl, &ctl.vin[vb], vp, err, 79) ||
+              !wait_mirror(&ctl, &ctl.m_vin[vb], vp, err, 79))
+            break;
+          const uint32_t fb = smem_addr(&ctl.kv_free[region]);
+          mbar_arrive(fb);
+          arrive_remote(peer_addr(fb, 1u));
+        } else {
+          // CTA 1's V buffer holds the tile (its own and the leader's copies)
+          if (!wait_bar(&ctl, &ctl.vin[vb], vp, err, 79)) break;
+          arrive_remote(peer_addr(smem_addr(&ctl.m_vin[vb]), 0u));
+        }
       }
     }
     __syncwarp();
@@ -620,6 +660,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     if (lane == 0) {
       const uint32_t q_bytes = (uint32_t)kHeadsPerCta * (uint32_t)args.head_dim * 2u;
       uint32_t q_empty_par = 1u;
+      int q_loads = 0;
       int next = span.r0;
       auto qrow_of = [&](int r, int* qrow) -> bool {
         const Row rv = load_row(rows, r);
@@ -645,204 +686,108 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         mbar_expect_tx(smem_addr(&ctl.q_full), q_bytes);
         for (int c = 0; c < nchunks; ++c)
           tma_load_2d(sQ + c * kQChunkBytes, &tm_q, c * 64, qrow, smem_addr(&ctl.q_full));
+        if (!leader) {
+          // CTA 1's Q of the row is in: tell the leader
+          if (!wait_bar(&ctl, &ctl.q_full, (uint32_t)(q_loads & 1), err, 74)) break;
+          arrive_remote(peer_addr(smem_addr(&ctl.m_q_full), 0u));
+        }
+        ++q_loads;
       }
     }
     __syncwarp();
-  } else if (warp == kPMmaWarp) {
+  } else if (warp == kPMmaWarp || warp == kPPvWarp) {
+    const bool qk_role = (warp == kPMmaWarp);
     if (leader) {
-      // ======================= MMA issuer (CTA 0) =======================
+      // ================= MMA issuers of the pair (CTA 0) =================
+      // One thread issues the QKs, another the PVs; each waits (bounded) for
+      // its inputs in both CTAs and issues in tile order.  The PV of tile t
+      // follows its QK through P(t) (the softmax read S(t)); QK(t + 2) reuses
+      // the S buffer of tile t after the softmax released it.
       if (lane == 0) {
-        const uint32_t idesc_qk = instr_desc(128, 64, kBf16, false, false);
-        const uint32_t idesc_pv = instr_desc(128, 256, kBf16, false, true);
-        uint32_t s_empty_par = 3u, q_full_par = 0u, o_free_par = 1u;
-        int tq = 0, tp = 0;  // tiles whose QK / PV are issued
-        int tv = 0;          // tiles whose V buffers are complete in both CTAs
-        bool vo = false, vm = false;
         bool ok = true;
-        TileCursor qc(rows, span), pc(rows, span);
-        int pending = 0, qg = 0;
-        bool q_own = false, q_m = false, s_own = false, s_m = false;
-        bool g_own = false, g_m = false;
-        bool p_own = false, p_m = false, o_own = false, o_m = false;
-        long long t_idle = clock64();
-        while (ok && (qc.valid || pending > 0)) {
-          bool progress = false;
-          // ---- V of the oldest tile whose QK is issued and V is not known
-          // complete: once both CTAs' V buffers hold it, every copy out of
-          // its gather regions has landed, so the leader releases them (its
-          // QK commit is the regions' other arrival) ----
-          if (tv < tq) {
-            const int vb = tv & 1;
-            const uint32_t vpar = (uint32_t)((tv >> 1) & 1);
-            if (!vo && (vo = mbar_test(smem_addr(&ctl.vin[vb]), vpar))) trace(tr, 1, 4098 + 4 * tv);
-            if (!vm && (vm = test_mirror(smem_addr(&ctl.m_vin[vb]), vpar)))
-              trace(tr, 1, 4099 + 4 * tv);
-            if (vo && vm) {
-              const uint32_t fb = smem_addr(&ctl.kv_free[tv % kNumRegions]);
-              mbar_arrive(fb);
-              arrive_remote(peer_addr(fb, 1u));
-              ++tv;
-              vo = vm = false;
-              progress = true;
-            }
-          }
-          // ---- PV of the oldest tile whose QK is issued ----
-          if (pending > 0) {
-            const uint32_t par = (uint32_t)(tp & 1);
-            const int vb = tp & 1;
-            if (!p_own && (p_own = mbar_test(smem_addr(&ctl.p_full), par))) trace(tr, 1, 4096 + 4 * tp);
-            if (!p_m && (p_m = test_mirror(smem_addr(&ctl.m_p_full), par))) trace(tr, 1, 4097 + 4 * tp);
-            if (!pc.first()) {
-              o_own = o_m = true;
-            } else {
-              if (!o_own) o_own = mbar_test(smem_addr(&ctl.o_free), o_free_par);
-              if (!o_m) o_m = test_mirror(smem_addr(&ctl.m_o_free), o_free_par);
-            }
-            if (p_own && p_m && tv > tp && o_own && o_m) {
-              if (pc.first()) o_free_par ^= 1u;
-              tc_fence_after();
-              trace(tr, 1, 4 * tp + 2);
-              issue_pv_pair(tmem + kPTmemO, sP, sV + vb * kVBufBytes, idesc_pv, pc.first());
-              commit_both(smem_addr(&ctl.pv_done[vb]));
-              if (pc.last()) commit_both(smem_addr(&ctl.o_full));
-              ++tp;
-              --pending;
-              pc.advance();
-              p_own = p_m = o_own = o_m = false;
-              progress = true;
-            }
-          }
-          // ---- QK of the next tile, one chunk group at a time ----
-          if (qc.valid) {
+        if (qk_role) {
+          const uint32_t idesc_qk = instr_desc(128, 64, kBf16, false, false);
+          TileCursor qc(rows, span);
+          int tq = 0, row_i = 0;
+          while (ok && qc.valid) {
             const int sb = tq & 1;
             const int region = tq % kNumRegions;
             if (qc.first()) {
-              if (!q_own) q_own = mbar_test(smem_addr(&ctl.q_full), q_full_par);
-              if (!q_m) q_m = test_mirror(smem_addr(&ctl.m_q_full), q_full_par);
-            } else {
-              q_own = q_m = true;
+              const uint32_t qp = (uint32_t)(row_i & 1);
+              ok = wait_bar(&ctl, &ctl.q_full, qp, err, 90) &&
+                   wait_mirror(&ctl, &ctl.m_q_full, qp, err, 91);
             }
-            if (q_own && q_m) {
-              const uint32_t sp = (s_empty_par >> sb) & 1u;
-              if (!s_own) s_own = mbar_test(smem_addr(&ctl.s_empty[sb]), sp);
-              if (!s_m) s_m = test_mirror(smem_addr(&ctl.m_s_empty[sb]), sp);
+            if (ok && tq >= 2) {
+              const uint32_t sp = (uint32_t)(((tq >> 1) - 1) & 1);
+              ok = wait_bar(&ctl, &ctl.s_empty[sb], sp, err, 92) &&
+                   wait_mirror(&ctl, &ctl.m_s_empty[sb], sp, err, 93);
             }
-            if (q_own && q_m && s_own && s_m) {
-              const uint32_t kp = (uint32_t)((tq / kNumRegions) & 1);
-              if (!g_own && (g_own = mbar_test(smem_addr(&ctl.kv_full[region][qg]), kp)))
-                trace(tr, 0, 4096 + 8 * tq + 2 * qg);
-              if (!g_m && (g_m = test_mirror(smem_addr(&ctl.m_kv_full[region][qg]), kp)))
-                trace(tr, 0, 4097 + 8 * tq + 2 * qg);
-              if (g_own && g_m) {
-                tc_fence_after();
-                if (qg == 0) trace(tr, 1, 4 * tq);
-                trace(tr, 3, 6144 + 8 * tq + 2 * qg);
-                issue_qk_pair<nchunks>(tmem + kPTmemS + 128u * sb, sQ,
-                                       sR0 + region * kRegionBytes, idesc_qk, qg);
-                trace(tr, 3, 6145 + 8 * tq + 2 * qg);
-                g_own = g_m = false;
-                progress = true;
-                if (++qg == 3) {
-                  trace(tr, 1, 4 * tq + 1);
-                  commit_both(smem_addr(&ctl.s_full[sb]));
-                  commit_both(smem_addr(&ctl.kv_free[region]));
-                  if (qc.last()) commit_both(smem_addr(&ctl.q_empty));
-                  if (qc.first()) q_full_par ^= 1u;
-                  s_empty_par ^= 1u << sb;
-                  ++tq;
-                  ++pending;
-                  qc.advance();
-                  qg = 0;
-                  q_own = q_m = s_own = s_m = false;
-                }
-              }
+            const uint32_t kp = (uint32_t)((tq / kNumRegions) & 1);
+            for (int g = 0; ok && g < 3; ++g) {
+              ok = wait_bar(&ctl, &ctl.kv_full[region][g], kp, err, 94) &&
+                   (g > 0 || wait_mirror(&ctl, &ctl.m_kv_full[region], kp, err, 95));
+              if (!ok) break;
+              tc_fence_after();
+              if (g == 0) trace(tr, 1, 4 * tq);
+              trace(tr, 3, 6144 + 8 * tq + 2 * g);
+              issue_qk_pair<nchunks>(tmem + kPTmemS + 128u * sb, sQ,
+                                     sR0 + region * kRegionBytes, idesc_qk, g);
+              trace(tr, 3, 6145 + 8 * tq + 2 * g);
             }
+            if (!ok) break;
+            trace(tr, 1, 4 * tq + 1);
+            commit_both(smem_addr(&ctl.s_full[sb]));
+            commit_both(smem_addr(&ctl.kv_free[region]));
+            if (qc.last()) {
+              commit_both(smem_addr(&ctl.q_empty));
+              ++row_i;
+            }
+            ++tq;
+            qc.advance();
           }
-          if (progress) {
-            t_idle = clock64();
-          } else {
-            if (ctl.abort) {
-              ok = false;
-              break;
+        } else {
+          const uint32_t idesc_pv = instr_desc(128, 256, kBf16, false, true);
+          TileCursor pc(rows, span);
+          int tp = 0, piece = 0;
+          while (ok && pc.valid) {
+            const int vb = tp & 1;
+            const uint32_t vp = (uint32_t)((tp >> 1) & 1);
+            const uint32_t pp = (uint32_t)(tp & 1);
+            ok = wait_bar(&ctl, &ctl.vin[vb], vp, err, 96) &&
+                 wait_mirror(&ctl, &ctl.m_vin[vb], vp, err, 97) &&
+                 wait_bar(&ctl, &ctl.p_full, pp, err, 98) &&
+                 wait_mirror(&ctl, &ctl.m_p_full, pp, err, 99);
+            if (ok && pc.first() && piece > 0) {
+              const uint32_t op = (uint32_t)((piece - 1) & 1);
+              ok = wait_bar(&ctl, &ctl.o_free, op, err, 100) &&
+                   wait_mirror(&ctl, &ctl.m_o_free, op, err, 101);
             }
-            if (clock64() - t_idle > kWaitCycles) {
-              record_error(err, SAS_ERR_DEVICE, 75, tp);
-              ctl.abort = 1;
-              ok = false;
-              break;
+            if (!ok) break;
+            tc_fence_after();
+            trace(tr, 1, 4 * tp + 2);
+            issue_pv_pair(tmem + kPTmemO, sP, sV + vb * kVBufBytes, idesc_pv, pc.first());
+            commit_both(smem_addr(&ctl.pv_done[vb]));
+            if (pc.last()) {
+              commit_both(smem_addr(&ctl.o_full));
+              ++piece;
             }
+            ++tp;
+            pc.advance();
           }
         }
-        // Drain: arrives in both CTAs once every MMA issued above has
-        // finished, so neither CTA releases TMEM under an in-flight MMA.
+        // Drain (both issuers): completes in both CTAs once every MMA issued
+        // above has finished, so neither CTA releases TMEM under an in-flight
+        // MMA.
         commit_both(smem_addr(&ctl.drain));
-        wait_bar(&ctl, &ctl.drain, 0u, err, 76);
+        wait_bar(&ctl, &ctl.drain, 0u, err, 102);
       }
       __syncwarp();
-    } else {
-      // ======================= relay (CTA 1) =======================
-      // Forwards, in order, each completed phase of this CTA's readiness
-      // barriers to the mirror barrier at the same offset in CTA 0.
-      if (lane == 0) {
-        int nrows = 0, ntiles = 0;
-        span_counts(rows, span, &nrows, &ntiles);
-        int iq = 0, ikv = 0, ise = 0, ipf = 0, iof = 0, ivn = 0;  // events forwarded
-        const int nkv = 3 * ntiles;
-        long long t_idle = clock64();
-        while (iq < nrows || ikv < nkv || ise < ntiles || ipf < ntiles || iof < nrows ||
-               ivn < ntiles) {
-          bool progress = false;
-          if (iq < nrows && mbar_test(smem_addr(&ctl.q_full), (uint32_t)(iq & 1))) {
-            arrive_remote(peer_addr(smem_addr(&ctl.m_q_full), 0u));
-            ++iq;
-            progress = true;
-          }
-          if (ikv < nkv) {
-            const int tt = ikv / 3, g = ikv % 3, region = tt % kNumRegions;
-            if (mbar_test(smem_addr(&ctl.kv_full[region][g]),
-                        (uint32_t)((tt / kNumRegions) & 1))) {
-              arrive_remote(peer_addr(smem_addr(&ctl.m_kv_full[region][g]), 0u));
-              ++ikv;
-              progress = true;
-            }
-          }
-          if (ise < ntiles &&
-              mbar_test(smem_addr(&ctl.s_empty[ise & 1]), (uint32_t)((ise >> 1) & 1))) {
-            arrive_remote(peer_addr(smem_addr(&ctl.m_s_empty[ise & 1]), 0u));
-            ++ise;
-            progress = true;
-          }
-          if (ivn < ntiles && mbar_test(smem_addr(&ctl.vin[ivn & 1]), (uint32_t)((ivn >> 1) & 1))) {
-            arrive_remote(peer_addr(smem_addr(&ctl.m_vin[ivn & 1]), 0u));
-            ++ivn;
-            progress = true;
-          }
-          if (ipf < ntiles && mbar_test(smem_addr(&ctl.p_full), (uint32_t)(ipf & 1))) {
-            arrive_remote(peer_addr(smem_addr(&ctl.m_p_full), 0u));
-            ++ipf;
-            progress = true;
-          }
-          if (iof < nrows && mbar_test(smem_addr(&ctl.o_free), (uint32_t)(iof & 1))) {
-            arrive_remote(peer_addr(smem_addr(&ctl.m_o_free), 0u));
-            ++iof;
-            progress = true;
-          }
-          if (progress) {
-            t_idle = clock64();
-          } else {
-            if (ctl.abort) break;
-            if (clock64() - t_idle > kWaitCycles) {
-              record_error(err, SAS_ERR_DEVICE, 77, ikv);
-              ctl.abort = 1;
-              break;
-            }
-          }
-        }
-        // The leader's last MMAs write this CTA's TMEM: wait for its drain.
-        wait_bar(&ctl, &ctl.drain, 0u, err, 78);
-      }
-      __syncwarp();
+    } else if (qk_role && lane == 0) {
+      // CTA 1: the leader's last MMAs write this CTA's TMEM; wait for its
+      // drain before the final cluster barrier and the release of TMEM.
+      wait_bar(&ctl, &ctl.drain, 0u, err, 78);
     }
+    __syncwarp();
   } else if (warp >= kPEpiWarp0) {
     // ======================= epilogue =======================
     const int ew = warp - kPEpiWarp0;
@@ -894,6 +839,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(smem_addr(&ctl.o_free));
+      __syncwarp();
+      if (!leader && lane == 0) arrive_remote(peer_addr(smem_addr(&ctl.m_o_free), 0u));
       ++k;
     }
   } else if (warp < 4) {
@@ -962,6 +909,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         }
         tc_fence_before();
         mbar_arrive(smem_addr(&ctl.s_empty[sb]));
+        __syncwarp();
+        if (!leader && lane == 0) arrive_remote(peer_addr(smem_addr(&ctl.m_s_empty[sb]), 0u));
         if (!__all_sync(0xffffffffu,
                         wait_bar(&ctl, &ctl.vfull[vr], (uint32_t)((t / kValidRing) & 1), err, 83))) {
           ok = false;
@@ -1045,6 +994,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         }
         tc_fence_before();
         mbar_arrive(smem_addr(&ctl.p_full));
+        __syncwarp();
+        if (!leader && lane == 0) arrive_remote(peer_addr(smem_addr(&ctl.m_p_full), 0u));
         if (threadIdx.x == 0) trace(tr, 2, 4 * t + 3);
       }
       if (!ok) break;

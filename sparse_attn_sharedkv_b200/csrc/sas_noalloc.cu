@@ -16,6 +16,8 @@
 //   address is looked up with cudaGetSymbolAddress once per device, on that
 //   device's first call (with that device current).  Make that first call
 //   before any stream capture.
+// * Each call builds its work plan on the host and copies it into the array
+//   with a stream-ordered copy from host memory, then launches the kernels.
 // * All calls on a device share the array and it keeps the last call's
 //   contents.  Nothing in it has to start at zero: the plan is rewritten by
 //   every call and each partial is written before it is read.  Calls that
@@ -65,10 +67,8 @@ extern "C" int sas_fwd_noalloc(const SasProblem* prob, const SasFwdParams* param
   void* scratch = nullptr;
   int rc = scratch_address(&scratch);
   if (rc != SAS_OK) return rc;
-  size_t need = 0;
-  rc = sas_fwd_workspace_size(prob, params->num_sms, &need);
-  if (rc != SAS_OK) return rc;
-  if (need > (size_t)SAS_NOALLOC_SCRATCH_BYTES) return SAS_ERR_WORKSPACE;
+  // sas_fwd_prepare plans once and returns SAS_ERR_WORKSPACE, before copying
+  // anything, when the plan and partials need more than the array holds.
   SasPlanInfo info;
   rc = sas_fwd_prepare(prob, params, scratch, SAS_NOALLOC_SCRATCH_BYTES, stream, &info);
   if (rc != SAS_OK) return rc;

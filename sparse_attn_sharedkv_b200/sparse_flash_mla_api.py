@@ -15,8 +15,7 @@ from typing import Optional, Tuple, Union
 
 import torch
 
-from .api import DEFAULT_CORE_NUM, _check_device_errors, _forward, _require, _restore_layout
-
+from .api import DEFAULT_CORE_NUM, _check_modes, _checked_forward, _restore_layout
 
 
 def sparse_flash_mla(
@@ -47,21 +46,11 @@ def sparse_flash_mla(
 ) -> Union[torch.Tensor, Tuple[torch.Tensor, torch.Tensor]]:
     """Sparse flash MLA forward (SWA / HCA / CSA)."""
     del seqused_q, core_num
-    _require(ori_mask_mode == 4, "only ori_mask_mode=4 supported")
-    _require(cmp_mask_mode == 3 or cmp_kv is None, "only cmp_mask_mode=3 supported")
-    _require(ori_win_right == 0, "only ori_win_right=0 supported")
-    _require(layout_kv == "PA_ND", "only layout_kv=PA_ND supported")
-    _require(layout_q in ("TND", "BSND"), f"unsupported layout_q={layout_q!r}")
-    err = torch.zeros(4, dtype=torch.int32, device=q.device) if _check_device_errors() else None
-    out_flat, lse_flat = _forward(
+    _check_modes(cmp_kv, ori_mask_mode, cmp_mask_mode, ori_win_right, layout_q, layout_kv)
+    out_flat, lse_flat = _checked_forward(
         q, ori_kv=ori_kv, cmp_kv=cmp_kv, cmp_sparse_indices=cmp_sparse_indices,
         ori_block_table=ori_block_table, cmp_block_table=cmp_block_table,
         cu_seqlens_q=cu_seqlens_q, seqused_kv=seqused_kv, sinks=sinks,
         softmax_scale=softmax_scale, cmp_ratio=cmp_ratio, ori_win_left=ori_win_left,
-        layout_q=layout_q, topk_cmp=topk_cmp, head_dim_v=head_dim_v, num_sms=num_sms, err=err)
-    if err is not None:
-        e = err.tolist()
-        if e[0] != 0:
-            raise RuntimeError(f"sas_fwd device check failed: code={e[0]} site={e[1]} "
-                               f"detail={e[2]} block={e[3]}")
+        layout_q=layout_q, topk_cmp=topk_cmp, head_dim_v=head_dim_v, num_sms=num_sms)
     return _restore_layout(q, out_flat, lse_flat, layout_q, return_softmax_lse)

@@ -150,13 +150,15 @@ D_QK, D_V, BLOCK = 576, 512, 64
 
 
 def baseline_case(i: int, device="cpu", *, scale_down: int = 1,
-                  minus_one_variant: bool = False) -> Case:
+                  minus_one_variant: bool = False, sequences: Optional[int] = None) -> Case:
     """Benchmark workload ``i`` (0-based index into the five configs).
 
     ``scale_down > 1`` shrinks the token / batch counts (keeping head count,
     head dims, block size and index density) for CPU-checkable parity runs.
     ``minus_one_variant`` shortens some sequences of the decode configs so the
-    ``-1`` index padding path is exercised.
+    ``-1`` index padding path is exercised.  ``sequences`` (config 4 only)
+    keeps that many of its 4096-token sequences, everything else unchanged
+    (profiling captures of a few GB).
     """
     device = torch.device(device)
     seed = i
@@ -226,6 +228,8 @@ def baseline_case(i: int, device="cpu", *, scale_down: int = 1,
 
     if i == 3:  # sparse prefill TND 8 x 4096, H=128, top-k 2048 from [0, pos]
         nseq, L, H, K = 8, 4096, 128, 2048
+        if sequences is not None:
+            nseq = int(sequences)
         if scale_down > 1:
             nseq = max(1, nseq // scale_down)
             L = max(256, L // scale_down)
