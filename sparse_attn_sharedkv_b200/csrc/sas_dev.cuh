@@ -26,6 +26,13 @@ constexpr float kRescaleThreshold = 8.0f;  // lazy O rescale (log2 units)
 
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 2 GHz
 
+// Independent S accumulators per tile: QK chunk c accumulates into partial
+// c % kQkPartials and the softmax sums the partials it reads from TMEM.
+#ifndef SAS_QK_PARTIALS
+#define SAS_QK_PARTIALS 4
+#endif
+constexpr int kQkPartials = SAS_QK_PARTIALS;
+
 // ---------------------------------------------------------------------------
 // PTX helpers.
 // ---------------------------------------------------------------------------

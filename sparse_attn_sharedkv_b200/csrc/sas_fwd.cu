@@ -75,7 +75,6 @@ constexpr int kEpiThreads = 32 * kNumEpiWarps;
 constexpr int kSoftmaxThreads = 32 * kNumSoftmaxWarps;
 constexpr int kProducerThreads = 32 * kNumProducerWarps;
 
-constexpr int kQkPartials = 4;     // independent S accumulators per tile (QK chains)
 // A K stage completes in three chunk groups (chunks 3g .. 3g + 2), each with
 // its own barrier, so QK starts on the first chunks while the rest land.
 constexpr int kChunkGroups = 3;
@@ -360,7 +359,8 @@ __device__ __forceinline__ void issue_qk_group(uint32_t d, uint32_t sQ, uint32_t
       if (i < nc) {
         const int c = c0 + i;
         const uint64_t off = (uint64_t)((c * kChunkBytes + ks * 32) >> 4);
-        mma_ws(d + 32u * (c & 3), dq + off, dk + off, idesc, (c < 4 && ks == 0) ? 0u : 1u);
+        mma_ws(d + 32u * (c % kQkPartials), dq + off, dk + off, idesc,
+               (c < kQkPartials && ks == 0) ? 0u : 1u);
       }
     }
   }
@@ -910,6 +910,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 : (size_t)rv.token * args.num_heads + group * kHeadsPerCta + m0;
       char* seg_base = split ? reinterpret_cast<char*>(args.o_partial + row0 * dv)
                              : reinterpret_cast<char*>(args.out) + row0 * dv * 2;
+#pragma unroll 1
       for (int c = 0; c < 8; ++c) {
         uint32_t v[32];
         tmem_ld32(obase + 32u * c, v);

@@ -373,9 +373,9 @@ __device__ __forceinline__ void issue_qk_pair(uint32_t d, uint32_t sQ, uint32_t 
     for (int i = 0; i < 3; ++i) {
       if (i < nc) {
         const int c = c0 + i;
-        mma2(d + 32u * (c & 3), dq + (uint64_t)((c * kQChunkBytes + ks * 32) >> 4),
+        mma2(d + 32u * (c % kQkPartials), dq + (uint64_t)((c * kQChunkBytes + ks * 32) >> 4),
              dk + (uint64_t)((c * kSlotBytes + ks * 32) >> 4), idesc,
-             (c < 4 && ks == 0) ? 0u : 1u);
+             (c < kQkPartials && ks == 0) ? 0u : 1u);
       }
     }
   }
@@ -894,7 +894,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           tmem_ld32(ts, sraw);
           tmem_wait_ld();
 #pragma unroll
-          for (int pp = 1; pp < 4; ++pp) {
+          for (int pp = 1; pp < kQkPartials; ++pp) {
 #pragma unroll
             for (int h16 = 0; h16 < 2; ++h16) {
               uint32_t t1[16];
