@@ -27,9 +27,11 @@ constexpr float kRescaleThreshold = 8.0f;  // lazy O rescale (log2 units)
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 2 GHz
 
 // Independent S accumulators per tile: QK chunk c accumulates into partial
-// c % kQkPartials and the softmax sums the partials it reads from TMEM.
+// c % kQkPartials and the softmax sums the partials it reads from TMEM.  Two
+// partials (two accumulation chains, both read before one TMEM wait) measured
+// faster than one or four on the benchmark workloads.
 #ifndef SAS_QK_PARTIALS
-#define SAS_QK_PARTIALS 4
+#define SAS_QK_PARTIALS 2
 #endif
 constexpr int kQkPartials = SAS_QK_PARTIALS;
 

@@ -32,8 +32,8 @@
 //
 // TMEM (512 columns): O[64 x 512] fp32 as two .ws M64 N256 accumulators
 // (cols 0-255, all 128 lanes); S[64 x 64] fp32 double-buffered, each buffer
-// as four partial sums over interleaved 64-dim chunks (cols 256-511), so the
-// 36 small QK MMAs form four independent accumulation chains.
+// as kQkPartials (2) partial sums over interleaved 64-dim chunks (cols
+// 256-511), so the 36 small QK MMAs form independent accumulation chains.
 // Shared memory: Q 72 KB and two K stages of 72 KB; P of a tile is written
 // into its stage's rope chunk (dims 512..575), which PV does not read.
 // 512 threads at 128 registers: every role fits without spills.
@@ -340,9 +340,9 @@ __device__ __forceinline__ void helper_rows(const FwdArgs& a, const CUtensorMap*
 }
 
 // Chunk group cg of S[sb] = Q K^T for the K tile at kb (chunks 3 cg ..
-// 3 cg + 2): chunk c accumulates into partial c % 4, so consecutive MMAs
-// rotate over the partials and four dependent chains overlap in the pipe;
-// a partial's first chunk (c < 4) starts it at ks = 0.  Descriptors are
+// 3 cg + 2): chunk c accumulates into partial c % kQkPartials, so
+// consecutive MMAs rotate over the partials and their dependent chains
+// overlap in the pipe; a partial's first chunk starts it at ks = 0.  Descriptors are
 // built once and advanced by constant offsets (all shared addresses are
 // below 256 KB, so the 14-bit address field never carries).
 template <int kChunks>
@@ -406,22 +406,6 @@ __device__ __forceinline__ SlotSrc resolve_tile(const FwdArgs& a, const Row& rv,
   if (m1mask != 0) *stopped = true;
   *valid = __ballot_sync(0xffffffffu, src.valid);
   return src;
-}
-
-// L2 prefetch of this warp's 16 compressed-cache key rows of a later tile (lane l: row
-// l % 16, lines [0, 5) or [5, row_bytes / 128) of it), so that the tile's
-// TMA gathers, issued once its stage is free, read L2 instead of HBM.
-__device__ __forceinline__ void prefetch_rows(const FwdArgs& a, const SlotSrc& src, int lane,
-                                              uint32_t row_bytes) {
-  // Window rows (cache 0) are recent and contiguous, typically L2-resident.
-  if (src.pool != 1 || src.row < 0) return;
-  const char* base = reinterpret_cast<const char*>(src.pool == 1 ? a.cmp_kv : a.ori_kv) +
-                     (size_t)src.row * row_bytes;
-  const int lines = (int)(row_bytes >> 7);
-  const int l0 = lane < 16 ? 0 : 5;
-  const int l1 = lane < 16 ? 5 : lines;
-  for (int l = l0; l < l1; ++l)
-    asm volatile("prefetch.global.L2 [%0];" ::"l"(base + l * 128) : "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -626,8 +610,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           stopped = __any_sync(0xffffffffu, m1);
         }
       }
-      // Tiles are resolved one ahead; head group 0 prefetches the next
-      // tile's rows into L2 (the other group reads the same rows).
+      // Tiles are resolved one ahead, so the index and block-table loads of
+      // the next tile overlap this tile's wait for its stage.
       uint32_t va = 0;
       SlotSrc nxt = resolve_tile(args, rv, qk, idx_row, ja, pw, lane, &stopped, &va, err);
       for (int j = ja; j < jb; ++j) {
@@ -637,7 +621,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           dump_slot(args, rv.token, j * kTileKeys + pw * 16 + lane, sa);
         if (j + 1 < jb) {
           nxt = resolve_tile(args, rv, qk, idx_row, j + 1, pw, lane, &stopped, &va, err);
-          if (group == 0) prefetch_rows(args, nxt, lane, row_bytes);
         }
         if (leader && lane == 0) trace(tr, 0, 3 * produced);
         if (!__all_sync(0xffffffffu,
@@ -991,12 +974,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         uint32_t sraw[32];
         {
-          // S = sum of the four partial accumulators, 16 columns at a time.
+          // S = sum of the partial accumulators (two: both loaded before one
+          // wait; four: 16 columns at a time).
           const uint32_t ts = tmem + lane_off + kTmemS + 128u * sb;
           tmem_ld32(ts, sraw);
-          tmem_wait_ld();
+          if constexpr (kQkPartials == 2) {
+            uint32_t t2[32];
+            tmem_ld32(ts + 32u, t2);
+            tmem_wait_ld();
 #pragma unroll
-          for (int pp = 1; pp < kQkPartials; ++pp) {
+            for (int i = 0; i < 32; ++i)
+              sraw[i] = __float_as_uint(__uint_as_float(sraw[i]) + __uint_as_float(t2[i]));
+          } else {
+            tmem_wait_ld();
+          }
+#pragma unroll
+          for (int pp = (kQkPartials == 2 ? 2 : 1); pp < kQkPartials; ++pp) {
 #pragma unroll
             for (int h16 = 0; h16 < 2; ++h16) {
               uint32_t t1[16];

@@ -359,7 +359,7 @@ __device__ __forceinline__ void prefetch_own_rows(const FwdArgs& a, const SlotSr
 }
 
 // Chunk group cg of S = Q K^T over the pair: chunk c of Q (64 heads) against
-// chunk slot c of the CTA's 32 key rows, into partial c % 4.
+// chunk slot c of the CTA's 32 key rows, into partial c % kQkPartials.
 template <int kChunks>
 __device__ __forceinline__ void issue_qk_pair(uint32_t d, uint32_t sQ, uint32_t region,
                                               uint32_t idesc, int cg) {
