@@ -665,7 +665,9 @@ def run_gpu(args):
                          "frac": ach / peak, "peak_source": f"{peak_src} (burst)",
                          "kernel": "sas_fwd_kernel", "kernel_ms": kern_ms,
                          "algorithmic_bytes": acct["bytes"], "algorithmic_flops": acct["flops"],
-                         "traffic": load_traffic(W.BASELINE_NAMES[cfg]) if ws == 1 else None,
+                         "traffic": (load_traffic(W.BASELINE_NAMES[cfg])
+                                     if ws == 1 and (args.sequences is None or cfg != 3)
+                                     else None),
                          "tensor_tflops": acct["flops"] / (kern_ms * 1e-3) / 1e12,
                          "hbm_gbs": acct["bytes"] / (kern_ms * 1e-3) / 1e9},
             "cpu_baseline": cpu,
