@@ -257,15 +257,31 @@ struct RowStream {
 
 // Diagnostic clock trace of one CTA (FwdArgs::trace_cta), compiled only into
 // the kernel instances launched with a trace buffer: 4 regions of 8192
-// entries: producer, MMA and softmax events per tile; in region 3 the
-// epilogue per row (from 0), MMA loop iterations (from 1024), the
-// chunk-group landings seen by the MMA issuer (from 2048), Q load issues
-// (from 4096) and Q arrivals (from 6144); in region 0 from 4096 the S
-// releases of the four softmax warps per tile.
+// entries.  Single-CTA kernel layout (each sub-range holds the events of as
+// many tiles / rows as fit; later ones are dropped, never written into the
+// next sub-range):
+//   region 0  [0, 4096) producer per tile (3 t: before the stage wait, stage
+//             free, loads issued); [4096, 8192) S released by softmax warp w
+//             of tile t (4 t + w)
+//   region 1  MMA per tile: 4 t QK start (S buffer free), 4 t + 1 QK issued,
+//             4 t + 2 / 4 t + 3 PV issue start / end
+//   region 2  [0, 6144) softmax per tile (4 t: K rows seen, + 1 max exchanged,
+//             + 2 P written, + 3 S seen); [6144, 8192) every CTA's start / end
+//             on the global timer (ns), 2 per CTA
+//   region 3  [0, 1024) rows: 3 k statistics handed on, 3 k + 1 / 3 k + 2
+//             epilogue start / end; [1024, 2048) MMA loop per tile (2 t QK
+//             committed, 2 t + 1 waiting for its S buffer); [2048, 4096) chunk
+//             group g of tile t seen by the MMA issuer (3 t + g); [4096, 6144)
+//             Q load issues; [6144, 8192) Q arrivals
 constexpr int kTraceRegion = 8192;
 __device__ __forceinline__ void trace(long long* tr, int region, int idx) {
   if (tr != nullptr && idx >= 0 && idx < kTraceRegion)
     tr[region * kTraceRegion + idx] = clock64();
+}
+// Entry base + idx of a region, written only while idx < limit.
+__device__ __forceinline__ void trace_in(long long* tr, int region, int base, int idx,
+                                         int limit) {
+  if (tr != nullptr && idx >= 0 && idx < limit) tr[region * kTraceRegion + base + idx] = clock64();
 }
 
 __device__ __forceinline__ uint64_t global_ns() {

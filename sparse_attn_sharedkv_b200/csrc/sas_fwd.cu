@@ -531,13 +531,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t va_cur = __ballot_sync(0xffffffffu, sa.valid);
           if (args.slot_dump != nullptr && lane < 16)
             dump_slot(args, rv.token, half * kTileKeys + pw * 16 + lane, sa);
-          if (leader && lane == 0) trace(tr, 0, 3 * produced);
+          if (leader && lane == 0) trace_in(tr, 0, 0, 3 * produced, 4096);
           if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.kv_empty[stage],
                                                 (kv_empty_par >> stage) & 1u, err, 2))) {
             ok = false;
             break;
           }
-          if (leader && lane == 0) trace(tr, 0, 3 * produced + 1);
+          if (leader && lane == 0) trace_in(tr, 0, 0, 3 * produced + 1, 4096);
           kv_empty_par ^= 1u << stage;
           uint32_t bar[kChunkGroups];
 #pragma unroll
@@ -574,7 +574,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
 #pragma unroll
           for (int cg = 0; cg < kChunkGroups; ++cg) cp_async_arrive_noinc(bar[cg]);
-          if (leader && lane == 0) trace(tr, 0, 3 * produced + 2);
+          if (leader && lane == 0) trace_in(tr, 0, 0, 3 * produced + 2, 4096);
           ++produced;
           stage ^= 1;
         }
@@ -622,13 +622,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (j + 1 < jb) {
           nxt = resolve_tile(args, rv, qk, idx_row, j + 1, pw, lane, &stopped, &va, err);
         }
-        if (leader && lane == 0) trace(tr, 0, 3 * produced);
+        if (leader && lane == 0) trace_in(tr, 0, 0, 3 * produced, 4096);
         if (!__all_sync(0xffffffffu,
                         wait_bar(&ctl, &ctl.kv_empty[stage], (kv_empty_par >> stage) & 1u, err, 2))) {
           ok = false;
           break;
         }
-        if (leader && lane == 0) trace(tr, 0, 3 * produced + 1);
+        if (leader && lane == 0) trace_in(tr, 0, 0, 3 * produced + 1, 4096);
         kv_empty_par ^= 1u << stage;
         uint32_t bar[kChunkGroups];
 #pragma unroll
@@ -647,7 +647,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                        lane, lsu, row_bytes, gran, &tm_ori, &tm_cmp, &tm_ori16, &tm_cmp16);
 #pragma unroll
         for (int cg = 0; cg < kChunkGroups; ++cg) cp_async_arrive_noinc(bar[cg]);
-        if (leader && lane == 0) trace(tr, 0, 3 * produced + 2);
+        if (leader && lane == 0) trace_in(tr, 0, 0, 3 * produced + 2, 4096);
         ++produced;
         stage ^= 1;
       }
@@ -722,7 +722,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!wait_bar(&ctl, &ctl.q_empty, q_empty_par, err, 1)) break;
         q_empty_par ^= 1u;
-        trace(tr, 3, 4096 + q_loads++);
+        trace_in(tr, 3, 4096, q_loads++, 2048);
         mbar_expect_tx(smem_addr(&ctl.q_full), q_bytes);
         for (int c = 0; c < nchunks; ++c)
           tma_load_2d(sQ + c * kChunkBytes, &tm_q, c * 64, qrow, smem_addr(&ctl.q_full));
@@ -796,10 +796,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else if (mbar_test(smem_addr(&ctl.q_full), q_full_par)) {
               q_ok = true;
               q_full_par ^= 1u;
-              trace(tr, 3, 6144 + q_seen++);
+              trace_in(tr, 3, 6144, q_seen++, 2048);
             }
           }
-          if (q_ok && !s_ok) trace(tr, 3, 1025 + 2 * qk_issued);
+          if (q_ok && !s_ok) trace_in(tr, 3, 1024, 2 * qk_issued + 1, 1024);
           if (q_ok && !s_ok &&
               mbar_test(smem_addr(&ctl.s_empty[qstage]), (s_empty_par >> qstage) & 1u)) {
             s_ok = true;
@@ -808,7 +808,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (s_ok &&
               mbar_test(smem_addr(&ctl.kv_full[qstage][qg]), (kv_full_par >> qstage) & 1u)) {
-            trace(tr, 3, 2048 + 3 * qk_issued + qg);
+            trace_in(tr, 3, 2048, 3 * qk_issued + qg, 2048);
             tc_fence_after();
             issue_qk_group<nchunks>(tmem + kTmemS + 128u * qstage, sQ,
                                     sK0 + qstage * kStageBytes, idesc_qk, qg);
@@ -819,7 +819,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               ++qk_issued;
               tc_commit(smem_addr(&ctl.s_full[qstage]));
               if (qc.last()) tc_commit(smem_addr(&ctl.q_empty));
-              trace(tr, 3, 1024 + 2 * qk_issued);
+              trace_in(tr, 3, 1024, 2 * qk_issued, 1024);
               qc.advance();
               qstage ^= 1;
               ++pending;
@@ -880,7 +880,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       wait_bar(&ctl, &ctl.fin_full[fp], (uint32_t)((k >> 1) & 1), err, 41)))
         break;
       tc_fence_after();
-      if (ew == 0 && lane == 0) trace(tr, 3, 3 * k + 1);
+      if (ew == 0 && lane == 0) trace_in(tr, 3, 0, 3 * k + 1, 1024);
       const float m_run = ctl.fin_m[fp][m];
       const float l_tot = ctl.fin_l[fp][0][m] + ctl.fin_l[fp][1][m];
       mbar_arrive(smem_addr(&ctl.fin_free[fp]));  // statistics read: the buffer is free
@@ -908,7 +908,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(smem_addr(&ctl.o_free));
-      if (ew == 0 && lane == 0) trace(tr, 3, 3 * k + 2);
+      if (ew == 0 && lane == 0) trace_in(tr, 3, 0, 3 * k + 2, 1024);
       ++k;
     }
   } else if (warp < kNumSoftmaxWarps) {
@@ -967,10 +967,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         sbuf ^= 1;
         if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.s_full[sb], (s_full_par >> sb) & 1u, err, 30))) { ok = false; break; }
         s_full_par ^= 1u << sb;
-        if (threadIdx.x == 0) trace(tr, 2, 4 * pv_count + 3);
+        if (threadIdx.x == 0) trace_in(tr, 2, 0, 4 * pv_count + 3, 6144);
         if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.kv_full[st][0], (kv_full_par >> st) & 1u, err, 31))) { ok = false; break; }
         kv_full_par ^= 1u << st;
-        if (threadIdx.x == 0) trace(tr, 2, 4 * pv_count);
+        if (threadIdx.x == 0) trace_in(tr, 2, 0, 4 * pv_count, 6144);
         tc_fence_after();
         uint32_t sraw[32];
         {
@@ -1004,7 +1004,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_before();
         mbar_arrive(smem_addr(&ctl.s_empty[sb]));
-        if (lane == 0) trace(tr, 0, 4096 + 4 * pv_count + warp);
+        if (lane == 0) trace_in(tr, 0, 4096, 4 * pv_count + warp, 4096);
         const uint32_t vb = (uint32_t)ctl.valid[st][2 * half] |
                             ((uint32_t)ctl.valid[st][2 * half + 1] << 16);
         float x[32];
@@ -1022,7 +1022,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!__all_sync(0xffffffffu, xw)) { ok = false; break; }
         mx = fmaxf(mx, ctl.red[xpar][half ^ 1][m]);
         xpar ^= 1;
-        if (threadIdx.x == 0) trace(tr, 2, 4 * pv_count + 1);
+        if (threadIdx.x == 0) trace_in(tr, 2, 0, 4 * pv_count + 1, 6144);
         const float m_new = fmaxf(m_run, mx);
         const bool rescale = (m_new - m_run) > kRescaleThreshold;  // NaN (-inf,-inf) -> false
         float alpha = 1.f;
@@ -1076,7 +1076,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_st();
         }
         tc_fence_before();
-        if (threadIdx.x == 0) trace(tr, 2, 4 * pv_count + 2);
+        if (threadIdx.x == 0) trace_in(tr, 2, 0, 4 * pv_count + 2, 6144);
         mbar_arrive(smem_addr(&ctl.p_full[st]));
         ++pv_count;
       }
@@ -1092,7 +1092,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (half == 0) ctl.fin_m[fp][m] = m_run;
       ctl.fin_l[fp][half][m] = l_run;
       mbar_arrive(smem_addr(&ctl.fin_full[fp]));
-      if (threadIdx.x == 0) trace(tr, 3, 3 * rows_done);
+      if (threadIdx.x == 0) trace_in(tr, 3, 0, 3 * rows_done, 1024);
       ++rows_done;
     }
   }
