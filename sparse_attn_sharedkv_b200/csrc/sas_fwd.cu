@@ -893,7 +893,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 : (size_t)rv.token * args.num_heads + group * kHeadsPerCta + m0;
       char* seg_base = split ? reinterpret_cast<char*>(args.o_partial + row0 * dv)
                              : reinterpret_cast<char*>(args.out) + row0 * dv * 2;
-#pragma unroll 1
       for (int c = 0; c < 8; ++c) {
         uint32_t v[32];
         tmem_ld32(obase + 32u * c, v);
