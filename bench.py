@@ -283,14 +283,18 @@ def run_reference(args):
             samples.append(t)
     value = statistics.median(vals) if vals else 0.0
     _, host = cpu_threads()
+    # time of one whole step (every token of the workload) at the sampled rate
+    step_flops = float(sum(flops_tok))
+    ms_step = step_flops / (value * 1e12) * 1e3 if value > 0 else None
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": None, "higher_is_better": True,
+        "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "strong" if args.gpus > 1 else "weak",
         "vs_baseline": None, "dtype": "f32 (bf16 inputs)", "data": "synthetic",
         "impl": "reference",
-        "config": {"workload": W.BASELINE_NAMES[args.config - 1], "device": "cpu"},
+        "config": {"workload": W.BASELINE_NAMES[args.config - 1], "device": "cpu",
+                   "ms_per_step": "one whole step of the workload at the sampled rate"},
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads,
                          "host_cores": host, "kind": "port",
                          "sample": f"{int(statistics.median(samples))} query tokens per step "
