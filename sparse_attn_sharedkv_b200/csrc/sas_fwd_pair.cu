@@ -571,7 +571,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   // issued) and the PV issuer (4 t + 2: inputs seen, 4 t + 3: issued);
   // region 2 softmax thread 0 (4 t: S seen, 4 t + 1: maximum exchanged, 4 t
   // + 2: P written, 4 t + 3: released), [6144, 8192) every CTA's start / end
-  // (global timer).
+  // (global timer); region 3 [0, 3072) chunk group g of tile t seen by the
+  // QK issuer (3 t + g), [4096, 6144) the PV issuer's V (2 t) and P (2 t + 1)
+  // seen, [6144, 8192) QK(t) seen complete by producer warp 4 (t).
   long long* tr = (kTrace && worker == args.trace_cta && rank == 0) ? args.trace : nullptr;
   if (kTrace && args.trace != nullptr && threadIdx.x == 0 && blockIdx.x < 1024)
     args.trace[2 * kTraceRegion + 6144 + 2 * blockIdx.x] = (long long)global_ns();
@@ -681,6 +683,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         if (j + 2 < jb)
           nxt = resolve_pair_tile(args, rv, qk, idx_row, (j + 2) * kTileKeys, slot_end, pw, rank,
                                   lane, &stopped, err);
+        // the index lines of the tile after next into L1, so that its
+        // resolve (one iteration later) reads L1 rather than L2
+        if (idx_row != nullptr && j + 4 < jb && lane < 5) {
+          const int c = (j + 4) * kTileKeys - rv.window + 32 * lane;
+          if (c >= 0 && c < qk.cmp)
+            asm volatile("prefetch.global.L1 [%0];" ::"l"(idx_row + c) : "memory");
+        }
         const int own_slot = j * kTileKeys + kOwnRows * rank + 16 * pw + lane;
         if (args.slot_dump != nullptr && lane < 16 && own_slot < slot_end)
           dump_slot(args, rv.token, own_slot, cur.src);
@@ -715,6 +724,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             ok = false;
             break;
           }
+          if (pw == 0 && lane == 0) trace_in(tr, 3, 6144, t - 1, 2048);
           load_pair_rows(args, prev, true, rank, pw, lane, sK + (s ^ 1) * kStageBytes, nchunks,
                          vbar(s ^ 1), maps, row_bytes, gran);
           if (pw == 0 && lane == 0) trace_in(tr, 0, 4096, 2 * (t - 1), 2048);
@@ -795,6 +805,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             for (int g = 0; ok && g < 3; ++g) {
               ok = wait_bar(&ctl, &ctl.kv_full[sb][g], kp, err, 94);
               if (!ok) break;
+              trace_in(tr, 3, 0, 3 * tq + g, 3072);
               tc_fence_after();
               issue_qk_pair<nchunks>(tmem + kPTmemS + 128u * sb, sQ, sK + sb * kStageBytes,
                                      idesc_qk, g);
@@ -817,9 +828,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           while (ok && pc.valid) {
             const int s = tp & 1;
             const uint32_t pp = (uint32_t)(tp & 1);
-            ok = wait_bar(&ctl, &ctl.v_full[s], (uint32_t)((tp >> 1) & 1), err, 96) &&
-                 wait_bar(&ctl, &ctl.p_full, pp, err, 98) &&
+            ok = wait_bar(&ctl, &ctl.v_full[s], (uint32_t)((tp >> 1) & 1), err, 96);
+            trace_in(tr, 3, 4096, 2 * tp, 2048);
+            ok = ok && wait_bar(&ctl, &ctl.p_full, pp, err, 98) &&
                  wait_mirror(&ctl, &ctl.m_p_full, pp, err, 99);
+            trace_in(tr, 3, 4096, 2 * tp + 1, 2048);
             if (ok && pc.first() && piece > 0) {
               const uint32_t op = (uint32_t)((piece - 1) & 1);
               ok = wait_bar(&ctl, &ctl.o_free, op, err, 100) &&
