@@ -46,12 +46,14 @@
 //   4-7    producers: slot -> (cache, position) -> block table -> row
 //          (golden.py:28-66, kernel.py:2606-2751), validity of the tile's
 //          128 slots, TMA of the CTA's 64 rows (16-row boxes or
-//          tile::gather4; cp.async for a 4-row group mixing the two caches)
-//          and of the peer's d_v columns once QK has read the stage
+//          tile::gather4; cp.async for a 4-row group mixing the two caches);
+//          the sources of the peer's rows go to the V warps
 //   8      CTA 0: QK issuer; TMEM allocation in both CTAs
 //   9      Q loader (TMA, next row's Q prefetched into L2)
 //   10     CTA 0: PV issuer
-//   12-15  epilogue: O / l -> out (or fp32 split partials) and the LSE
+//   12-15  V gather (the CTA's d_v columns of the peer's rows, once QK has
+//          read the stage) and epilogue: O / l -> out (or fp32 split
+//          partials) and the LSE
 //
 // Every wait is bounded: on timeout the thread records an error, raises its
 // CTA's abort flag and leaves its loop; both CTAs then meet at the final
@@ -105,12 +107,16 @@ struct PairCtl {
   uint64_t o_full, o_free, m_o_free, drain;
   uint64_t xbar[2];
   uint64_t fin_full[2], fin_free[2];
+  uint64_t vsrc_full[2], vsrc_free[2];  // peer sources of a tile, producers -> V warps
   uint32_t tmem_base;
   volatile int abort;
   uint32_t valid[kValidRing][4];     // word w: slots 32 w .. 32 w + 31 of the tile
   float red[2][2][kHeadsPerCta];
   float fin_m[2][kHeadsPerCta];
-  float fin_l[2][2][kHeadsPerCta];
+  // Softmax sum of each head, both key halves added into it: two addends
+  // from zero give the same float in either order.
+  float fin_l[2][kHeadsPerCta];
+  int32_t vsrc[2][kOwnRows];         // packed sources of the peer's rows of a tile
 };
 static_assert(kPSmemCtl + (int)sizeof(PairCtl) <= kPSmemDynamic, "shared memory budget");
 
@@ -441,12 +447,25 @@ __device__ __forceinline__ void issue_pv_pair(uint32_t o, uint32_t p_lo, uint32_
   }
 }
 
+// A slot source in one int: 2 row + cache, -2 - cache for an unmapped page,
+// -1 for a masked slot.
+__device__ __forceinline__ int32_t pack_src(const SlotSrc& s) {
+  if (s.pool < 0) return -1;
+  return s.row >= 0 ? 2 * s.row + s.pool : -2 - s.pool;
+}
+__device__ __forceinline__ SlotSrc unpack_src(int32_t v) {
+  if (v >= 0) return SlotSrc{v >> 1, v & 1, true};
+  if (v == -1) return SlotSrc{-1, -1, false};
+  return SlotSrc{-1, -2 - v, true};
+}
+
 // Walks the pair tiles of a worker span in plan order: tile j .. j + 1 of a
 // (row, piece) [ja, jb), skipping rows without key tiles.  first / last: the
 // pair tile opens / closes its (row, piece).
 struct PairCursor {
   RowStream rs;
   Span span;
+  Row row;
   int r, j, ja, jb;
   bool valid;
   __device__ __forceinline__ PairCursor(const int* rows, const Span& sp)
@@ -456,8 +475,8 @@ struct PairCursor {
   __device__ __forceinline__ void next_row() {
     valid = false;
     while (span.r0 >= 0 && ++r <= span.r1) {
-      const Row rv = rs.take(r);
-      const int tiles = row_tiles(rv);
+      row = rs.take(r);
+      const int tiles = row_tiles(row);
       ja = (r == span.r0) ? span.t0 : 0;
       jb = (r == span.r1) ? span.t1 : (tiles > 0 ? tiles : 1);
       if (tiles > 0 && ja < jb) {
@@ -607,6 +626,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     mbar_init(smem_addr(&ctl.o_free), kPEpiThreads);
     mbar_init(smem_addr(&ctl.m_o_free), 4);
     mbar_init(smem_addr(&ctl.drain), 2);  // one commit from each MMA issuer
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_addr(&ctl.vsrc_full[i]), 4);
+      mbar_init(smem_addr(&ctl.vsrc_free[i]), 4);
+      for (int h = 0; h < kHeadsPerCta; ++h) ctl.fin_l[i][h] = 0.f;
+    }
     ctl.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -631,9 +655,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
 
   if (warp >= kPProducerWarp0 && warp < kPProducerWarp0 + 4) {
     // ======================= producers =======================
-    // Per pair tile t (stage t % 2): valid bits, then, once PV(t - 2) has
-    // released the stage, the CTA's 64 rows; then, once QK(t - 1) has read
-    // its stage, the d_v columns of the peer's rows of tile t - 1.
+    // Per pair tile t (stage t % 2): valid bits, the peer's sources for the V
+    // warps, then, once PV(t - 2) has released the stage, the CTA's 64 rows.
     const int pw = warp - kPProducerWarp0;
     const int D = args.head_dim;
     const uint32_t row_bytes = (uint32_t)D * 2u;
@@ -641,10 +664,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     const PairMaps maps{&tm_ori, &tm_cmp, &tm_ori16, &tm_cmp16};
     // the leader's barriers (shared::cluster addresses)
     auto kbar = [&](int s) { return peer_addr(smem_addr(&ctl.kv_full[s][0]), 0u); };
-    auto vbar = [&](int s) { return peer_addr(smem_addr(&ctl.v_full[s]), 0u); };
     int t = 0;  // pair tiles of the span so far
     bool ok = true;
-    SlotSrc prev{-1, -1, false};
     RowStream rs(rows, span.r0, span.r1);
     for (int r = span.r0; ok && span.r0 >= 0 && r <= span.r1; ++r) {
       const Row rv = rs.take(r);
@@ -707,6 +728,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           ctl.valid[vr][pw] = cur.valid32;
           mbar_arrive(smem_addr(&ctl.vfull[vr]));
         }
+        // the peer's sources of tile t for the V warps (vsrc[s] is free once
+        // they have read tile t - 2's)
+        if (t >= 2 && !__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.vsrc_free[s],
+                                                        (uint32_t)(((t >> 1) - 1) & 1), err, 75))) {
+          ok = false;
+          break;
+        }
+        if (lane >= 16) ctl.vsrc[s][16 * pw + lane - 16] = pack_src(cur.src);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_addr(&ctl.vsrc_full[s]));
         // the stage: PV(t - 2) has read it
         if (t >= 2 && !__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.pv_done[s],
                                                         (uint32_t)(((t >> 1) - 1) & 1), err, 71))) {
@@ -717,27 +748,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         load_pair_rows(args, cur.src, false, rank, pw, lane, sK + s * kStageBytes, nchunks,
                        kbar(s), maps, row_bytes, gran);
         if (pw == 0 && lane == 0) trace_in(tr, 0, 0, 3 * t + 2, 4096);
-        if (t >= 1) {
-          // V columns of tile t - 1 once its QK has read stage s ^ 1
-          if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.qk_done[s ^ 1],
-                                                (uint32_t)(((t - 1) >> 1) & 1), err, 72))) {
-            ok = false;
-            break;
-          }
-          if (pw == 0 && lane == 0) trace_in(tr, 3, 6144, t - 1, 2048);
-          load_pair_rows(args, prev, true, rank, pw, lane, sK + (s ^ 1) * kStageBytes, nchunks,
-                         vbar(s ^ 1), maps, row_bytes, gran);
-          if (pw == 0 && lane == 0) trace_in(tr, 0, 4096, 2 * (t - 1), 2048);
-        }
-        prev = cur.src;
       }
-    }
-    if (ok && t >= 1) {
-      const int s = (t - 1) & 1;
-      if (__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.qk_done[s],
-                                           (uint32_t)(((t - 1) >> 1) & 1), err, 73)))
-        load_pair_rows(args, prev, true, rank, pw, lane, sK + s * kStageBytes, nchunks, vbar(s),
-                       maps, row_bytes, gran);
     }
     cp_async_wait_all();
   } else if (warp == kPQWarp) {
@@ -868,7 +879,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     }
     __syncwarp();
   } else if (warp >= kPEpiWarp0) {
-    // ======================= epilogue =======================
+    // ================= V gather and epilogue =================
+    // Per pair tile t, epilogue warp ew gathers the d_v columns this CTA
+    // supplies to PV of the peer's rows 16 ew .. 16 ew + 15 (sources from the
+    // producers), once QK(t) has read stage t % 2; after the last tile of a
+    // (row, piece), once its PV is done: O / l -> out (or the fp32 split
+    // partials) and the LSE.
     const int ew = warp - kPEpiWarp0;
     const int half = ew >> 1;
     const int m0 = (ew & 1) * 32;
@@ -876,52 +892,72 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     const int dv = args.head_dim_v;
     const uint32_t obase = tmem + ((uint32_t)(ew * 32) << 16) + kPTmemO;
     const bool live = group * kHeadsPerCta + m < args.num_heads;
-    int k = 0;
-    RowStream rs(rows, span.r0, span.r1);
-    for (int r = span.r0; span.r0 >= 0 && r <= span.r1; ++r) {
-      const Row rv = rs.take(r);
-      const int tiles = row_tiles(rv);
-      const int ja = (r == span.r0) ? span.t0 : 0;
-      const int jb = (r == span.r1) ? span.t1 : (tiles > 0 ? tiles : 1);
-      if (tiles == 0 || ja >= jb) continue;
-      const int fp = k & 1;
-      if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.o_full, (uint32_t)(k & 1), err, 80)))
-        break;
-      if (!__all_sync(0xffffffffu,
-                      wait_bar(&ctl, &ctl.fin_full[fp], (uint32_t)((k >> 1) & 1), err, 81)))
-        break;
-      tc_fence_after();
-      const float m_run = ctl.fin_m[fp][m];
-      const float l_tot = ctl.fin_l[fp][0][m] + ctl.fin_l[fp][1][m];
-      mbar_arrive(smem_addr(&ctl.fin_free[fp]));
-      const float inv = (l_tot > 0.f) ? 1.f / l_tot : 0.f;
-      const float lse = (m_run + log2f(l_tot)) * kLn2;
-      const bool split = rv.partial_base >= 0;
-      const int piece = (r == span.r0) ? span.piece0 : 0;
-      const size_t hrow = split ? (size_t)(rv.partial_base + piece) * args.num_heads +
-                                      group * kHeadsPerCta + m
-                                : (size_t)rv.token * args.num_heads + group * kHeadsPerCta + m;
-      char* row_base = split ? reinterpret_cast<char*>(args.o_partial + hrow * dv)
-                             : reinterpret_cast<char*>(args.out) + hrow * dv * 2;
-#pragma unroll 1
-      for (int c = 0; c < 8; ++c) {
-        uint32_t v[32];
-        tmem_ld32(obase + 32u * c, v);
-        tmem_wait_ld();
-        if (live) epi_direct<kBf16>(v, c, half, inv, split, row_base);
-      }
-      if (half == 0 && live) {
-        if (split)
-          args.lse_partial[hrow] = lse;
-        else
-          args.lse[hrow] = lse;
-      }
-      tc_fence_before();
-      mbar_arrive(smem_addr(&ctl.o_free));
+    const PairMaps maps{&tm_ori, &tm_cmp, &tm_ori16, &tm_cmp16};
+    const uint32_t row_bytes = (uint32_t)args.head_dim * 2u;
+    const int gran = args.head_dim >> 3;
+    PairCursor ec(rows, span);
+    int t = 0, k = 0;
+    while (ec.valid) {
+      const int s = t & 1;
+      const uint32_t tp = (uint32_t)((t >> 1) & 1);
+      if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.vsrc_full[s], tp, err, 87))) break;
+      SlotSrc src{-1, -1, false};
+      if (lane >= 16) src = unpack_src(ctl.vsrc[s][16 * ew + lane - 16]);
       __syncwarp();
-      if (!leader && lane == 0) arrive_remote(peer_addr(smem_addr(&ctl.m_o_free), 0u));
-      ++k;
+      if (lane == 0) mbar_arrive(smem_addr(&ctl.vsrc_free[s]));
+      if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.qk_done[s], tp, err, 72))) break;
+      if (ew == 0 && lane == 0) trace_in(tr, 3, 6144, t, 2048);
+      load_pair_rows(args, src, true, rank, ew, lane, sK + s * kStageBytes, nchunks,
+                     peer_addr(smem_addr(&ctl.v_full[s]), 0u), maps, row_bytes, gran);
+      if (ew == 0 && lane == 0) trace_in(tr, 0, 4096, 2 * t, 2048);
+      if (ec.last()) {
+        const Row& rv = ec.row;
+        const int fp = k & 1;
+        if (!__all_sync(0xffffffffu, wait_bar(&ctl, &ctl.o_full, (uint32_t)(k & 1), err, 80)))
+          break;
+        if (!__all_sync(0xffffffffu,
+                        wait_bar(&ctl, &ctl.fin_full[fp], (uint32_t)((k >> 1) & 1), err, 81)))
+          break;
+        tc_fence_after();
+        const float m_run = ctl.fin_m[fp][m];
+        const float l_tot = ctl.fin_l[fp][m];
+        // both epilogue threads of head m have read the sum: clear it for the
+        // row after next
+        asm volatile("bar.sync 1, %0;" ::"r"(kPEpiThreads) : "memory");
+        if (half == 0) ctl.fin_l[fp][m] = 0.f;
+        mbar_arrive(smem_addr(&ctl.fin_free[fp]));
+        const float inv = (l_tot > 0.f) ? 1.f / l_tot : 0.f;
+        const float lse = (m_run + log2f(l_tot)) * kLn2;
+        const bool split = rv.partial_base >= 0;
+        const int piece = (ec.r == span.r0) ? span.piece0 : 0;
+        const size_t hrow = split ? (size_t)(rv.partial_base + piece) * args.num_heads +
+                                        group * kHeadsPerCta + m
+                                  : (size_t)rv.token * args.num_heads + group * kHeadsPerCta + m;
+        char* row_base = split ? reinterpret_cast<char*>(args.o_partial + hrow * dv)
+                               : reinterpret_cast<char*>(args.out) + hrow * dv * 2;
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {
+          uint32_t v[32];
+          tmem_ld32(obase + 32u * c, v);
+          tmem_wait_ld();
+          if (live) epi_direct<kBf16>(v, c, half, inv, split, row_base);
+        }
+        if (half == 0 && live) {
+          if (split)
+            args.lse_partial[hrow] = lse;
+          else
+            args.lse[hrow] = lse;
+        }
+        tc_fence_before();
+        mbar_arrive(smem_addr(&ctl.o_free));
+        __syncwarp();
+        if (!leader && lane == 0) arrive_remote(peer_addr(smem_addr(&ctl.m_o_free), 0u));
+        ++k;
+      }
+      ++t;
+      ec.advance();
     }
+    cp_async_wait_all();
   } else if (warp < 4) {
     // ======================= softmax =======================
     // Thread L: head m = L % 64 of the CTA, key half L / 64 (keys 64 half ..
@@ -1088,7 +1124,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                                             (uint32_t)(((rows_done >> 1) & 1) ^ 1), err, 86)))
         break;
       if (half == 0) ctl.fin_m[fp][m] = m_run;
-      ctl.fin_l[fp][half][m] = l_run;
+      atomicAdd(&ctl.fin_l[fp][m], l_run);
       mbar_arrive(smem_addr(&ctl.fin_full[fp]));
       ++rows_done;
     }
