@@ -316,6 +316,15 @@ __device__ __forceinline__ bool wait_bar(CtlT* ctl, uint64_t* bar, uint32_t pari
   }
 }
 
+// 2^x by the MUFU approximation (PTX ex2.approx.ftz.f32: relative error
+// about 2^-22, results below 2^-126 flushed to zero; 2^-inf = 0): the
+// softmax's P, which is rounded to bf16 / fp16 right after.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 template <bool kBf16>
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
   if constexpr (kBf16) {

@@ -1041,8 +1041,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const int i = 8 * g + 2 * q;
-            const float p0 = exp2f(x[i] - m_use);
-            const float p1 = exp2f(x[i + 1] - m_use);
+            const float p0 = ex2_approx(x[i] - m_use);
+            const float p1 = ex2_approx(x[i + 1] - m_use);
             lsum += p0 + p1;
             pk[q] = pack2<kBf16>(p0, p1);
           }

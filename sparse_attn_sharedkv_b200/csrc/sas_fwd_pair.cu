@@ -87,9 +87,13 @@ constexpr int kPSmemDynamic = 232448;             // the per-block opt-in maximu
 constexpr int kValidRing = 4;                     // tiles whose valid bits are in flight
 constexpr int kRopeSlot = 8;                      // slot of P's key half 0 once QK read it
 
+// One S accumulator per tile: with 64 keys per thread the softmax reads S in
+// one round of TMEM loads (measured faster than two partial sums).
+constexpr int kPairQkPartials = 1;
+
 constexpr uint32_t kPTmemCols = 512;
 constexpr uint32_t kPTmemO = 0;    // O: 2 x 128 columns (N = 256 accumulators)
-constexpr uint32_t kPTmemS = 256;  // S: 2 buffers x 2 partials x 64 columns
+constexpr uint32_t kPTmemS = 256;  // S: 2 buffers of 128 columns (partial p at + 64 p)
 
 struct PairCtl {
   // Leader only: all rows of stage s, chunk group g, of both CTAs landed.
@@ -401,7 +405,7 @@ __device__ __forceinline__ void load_pair_rows(const FwdArgs& a, const SlotSrc& 
 }
 
 // Chunk group cg of S = Q K^T over the pair: chunk c of Q (64 heads) against
-// chunk slot c of the CTA's 64 key rows, into partial c % kQkPartials (64
+// chunk slot c of the CTA's 64 key rows, into partial c % kPairQkPartials (64
 // TMEM columns each).
 template <int kChunks>
 __device__ __forceinline__ void issue_qk_pair(uint32_t d, uint32_t sQ, uint32_t stage,
@@ -416,9 +420,9 @@ __device__ __forceinline__ void issue_qk_pair(uint32_t d, uint32_t sQ, uint32_t 
     for (int i = 0; i < 3; ++i) {
       if (i < nc) {
         const int c = c0 + i;
-        mma2(d + 64u * (c % kQkPartials), dq + (uint64_t)((c * kQChunkBytes + ks * 32) >> 4),
+        mma2(d + 64u * (c % kPairQkPartials), dq + (uint64_t)((c * kQChunkBytes + ks * 32) >> 4),
              dk + (uint64_t)((c * kSlotBytes + ks * 32) >> 4), idesc,
-             (c < kQkPartials && ks == 0) ? 0u : 1u);
+             (c < kPairQkPartials && ks == 0) ? 0u : 1u);
       }
     }
   }
@@ -588,11 +592,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   // wait, 3 t + 1: stage free, 3 t + 2: rows issued), [4096, 6144) 2 t: V
   // gather of tile t issued; region 1 the QK issuer (4 t: start, 4 t + 1:
   // issued) and the PV issuer (4 t + 2: inputs seen, 4 t + 3: issued);
-  // region 2 softmax thread 0 (4 t: S seen, 4 t + 1: maximum exchanged, 4 t
-  // + 2: P written, 4 t + 3: released), [6144, 8192) every CTA's start / end
-  // (global timer); region 3 [0, 3072) chunk group g of tile t seen by the
-  // QK issuer (3 t + g), [4096, 6144) the PV issuer's V (2 t) and P (2 t + 1)
-  // seen, [6144, 8192) QK(t) seen complete by producer warp 4 (t).
+  // region 2 softmax thread 0 ([0, 4000) 4 t: S seen, 4 t + 1: maximum
+  // exchanged, 4 t + 2: P written, 4 t + 3: released; [4000, 6000) 2 t: S
+  // in registers, 2 t + 1: valid bits seen), [6144, 8192) every CTA's start
+  // / end (global timer); region 3 [0, 3072) chunk group g of tile t seen by
+  // the QK issuer (3 t + g), [3072, 4096) softmax thread 96 at its maximum
+  // exchange (t), [4096, 6144) the PV issuer's V (2 t) and P (2 t + 1) seen,
+  // [6144, 8192) QK(t) seen complete by V warp 12 (t).
   long long* tr = (kTrace && worker == args.trace_cta && rank == 0) ? args.trace : nullptr;
   if (kTrace && args.trace != nullptr && threadIdx.x == 0 && blockIdx.x < 1024)
     args.trace[2 * kTraceRegion + 6144 + 2 * blockIdx.x] = (long long)global_ns();
@@ -1005,28 +1011,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           break;
         }
         tc_fence_after();
-        if (threadIdx.x == 0) trace_in(tr, 2, 0, 4 * t, 6144);
+        if (threadIdx.x == 0) trace_in(tr, 2, 0, 4 * t, 4000);
         float x[64];
         {
           const uint32_t ts = tmem + lane_off + kPTmemS + 128u * sb;
+          if constexpr (kPairQkPartials == 1) {
+            // both 32-column halves in flight, one wait
+            uint32_t a0[32], a1[32];
+            tmem_ld32(ts, a0);
+            tmem_ld32(ts + 32u, a1);
+            tmem_wait_ld();
 #pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2) {
-            uint32_t a0[32];
-            tmem_ld32(ts + 32u * h2, a0);
-            if constexpr (kQkPartials == 2) {
-              uint32_t a1[32];
+            for (int i = 0; i < 32; ++i) {
+              x[i] = __uint_as_float(a0[i]);
+              x[32 + i] = __uint_as_float(a1[i]);
+            }
+          } else {
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+              uint32_t a0[32], a1[32];
+              tmem_ld32(ts + 32u * h2, a0);
               tmem_ld32(ts + 64u + 32u * h2, a1);
               tmem_wait_ld();
 #pragma unroll
               for (int i = 0; i < 32; ++i)
                 x[32 * h2 + i] = __uint_as_float(a0[i]) + __uint_as_float(a1[i]);
-            } else {
-              tmem_wait_ld();
-#pragma unroll
-              for (int i = 0; i < 32; ++i) x[32 * h2 + i] = __uint_as_float(a0[i]);
             }
           }
         }
+        if (threadIdx.x == 0) trace_in(tr, 2, 4000, 2 * t, 2000);
         tc_fence_before();
         mbar_arrive(smem_addr(&ctl.s_empty[sb]));
         __syncwarp();
@@ -1036,6 +1049,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           ok = false;
           break;
         }
+        if (threadIdx.x == 0) trace_in(tr, 2, 4000, 2 * t + 1, 2000);
         const uint32_t va = ctl.valid[vr][2 * half];
         const uint32_t vb = ctl.valid[vr][2 * half + 1];
         float mx = -INFINITY;
@@ -1047,6 +1061,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           mx = fmaxf(mx, v);
         }
         ctl.red[xpar][half][m] = mx;
+        if (threadIdx.x == 96) trace_in(tr, 3, 3072, t, 1024);
         mbar_arrive(smem_addr(&ctl.xbar[xpar]));
         const bool xw = wait_bar(&ctl, &ctl.xbar[xpar], (xph >> xpar) & 1u, err, 84);
         xph ^= 1u << xpar;
@@ -1057,7 +1072,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         // every softmax thread has read valid[vr]: the producers may reuse it
         if (threadIdx.x == 0) {
           mbar_arrive(smem_addr(&ctl.vfree[vr]));
-          trace_in(tr, 2, 0, 4 * t + 1, 6144);
+          trace_in(tr, 2, 0, 4 * t + 1, 4000);
         }
         mx = fmaxf(mx, ctl.red[xpar][half ^ 1][m]);
         xpar ^= 1;
@@ -1088,8 +1103,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const int i = 8 * g + 2 * q;
-            const float p0 = exp2f(x[i] - m_use);
-            const float p1 = exp2f(x[i + 1] - m_use);
+            const float p0 = ex2_approx(x[i] - m_use);
+            const float p1 = ex2_approx(x[i + 1] - m_use);
             lsum += p0 + p1;
             pk[q] = pack2<kBf16>(p0, p1);
           }
@@ -1097,7 +1112,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         }
         l_run += lsum;
         fence_proxy_async();
-        if (threadIdx.x == 0) trace_in(tr, 2, 0, 4 * t + 2, 6144);
+        if (threadIdx.x == 0) trace_in(tr, 2, 0, 4 * t + 2, 4000);
         if (rescale_o) {
           tc_fence_after();
 #pragma unroll 1
@@ -1116,7 +1131,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         mbar_arrive(smem_addr(&ctl.p_full));
         __syncwarp();
         if (!leader && lane == 0) arrive_remote(m_p_full);
-        if (threadIdx.x == 0) trace_in(tr, 2, 0, 4 * t + 3, 6144);
+        if (threadIdx.x == 0) trace_in(tr, 2, 0, 4 * t + 3, 4000);
       }
       if (!ok) break;
       const int fp = rows_done & 1;
