@@ -76,6 +76,16 @@ def load_peaks():
         return dict(FALLBACK_PEAKS), "fallback"
 
 
+def attention_kernel_name(info):
+    """The attention kernel libsas launches for a plan: the CTA-pair kernel for
+    two head groups (65..128 heads) unless SAS_FWD_KERNEL=single or the
+    cp.async gather mode is chosen, else the one-CTA-per-head-group kernel."""
+    pair = (info is not None and info.head_groups == 2
+            and os.environ.get("SAS_FWD_KERNEL") != "single"
+            and os.environ.get("SAS_GATHER") != "lsu")
+    return "sas_pair_kernel" if pair else "sas_fwd_kernel"
+
+
 def load_traffic(workload: str):
     """DRAM bytes per launch of the attention kernel from the committed ncu
     summary (profiles/traffic.txt: ``<workload> <bytes>`` lines), or None."""
@@ -667,7 +677,7 @@ def run_gpu(args):
                             + ("; each rank copies its own shard" if ws > 1 else "")},
             "roofline": {"bound": bound, "achieved": ach, "peak": peak, "unit": unit,
                          "frac": ach / peak, "peak_source": f"{peak_src} (burst)",
-                         "kernel": "sas_fwd_kernel", "kernel_ms": kern_ms,
+                         "kernel": attention_kernel_name(info), "kernel_ms": kern_ms,
                          "algorithmic_bytes": acct["bytes"], "algorithmic_flops": acct["flops"],
                          "traffic": (load_traffic(W.BASELINE_NAMES[cfg])
                                      if ws == 1 and (args.sequences is None or cfg != 3)

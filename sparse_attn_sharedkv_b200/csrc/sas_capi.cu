@@ -211,12 +211,13 @@ extern "C" int sas_fwd_execute(const SasProblem* prob, const SasFwdParams* param
   a.slot_dump_cap = f.slot_dump != nullptr ? f.slot_dump_cap : 0;
   int rc = SAS_OK;
   if (phases & SAS_PHASE_ATTN) {
-    // Two head groups (65..128 heads) run on one CTA per head group, or on
-    // CTA pairs issuing cta_group::2 MMAs when SAS_FWD_KERNEL=pair (read at
-    // each call).
+    // Two head groups (65..128 heads) run on CTA pairs issuing cta_group::2
+    // MMAs over 128-key tiles, or on one CTA per 64-head group with
+    // SAS_FWD_KERNEL=single or in the cp.async gather mode (read at each
+    // call).
     const char* ek = getenv("SAS_FWD_KERNEL");
-    const bool pair = ek != nullptr && strcmp(ek, "pair") == 0;
-    if (info.head_groups == 2 && pair)
+    const bool single = (ek != nullptr && strcmp(ek, "single") == 0) || a.gather == 0;
+    if (info.head_groups == 2 && !single)
       rc = sas::launch_fwd_pair(a, info.num_workers, stream);
     else
       rc = sas::launch_fwd(a, info.num_workers * info.head_groups, stream);
