@@ -109,7 +109,7 @@ struct PairCtl {
   uint64_t q_full, q_empty;
   uint64_t s_full[2], s_empty[2], m_s_empty[2];
   uint64_t o_full, o_free, m_o_free, drain;
-  uint64_t xbar[2];
+  uint64_t xbar[2][2];                // [parity][warp pair: warps w, w + 2 share heads]
   uint64_t fin_full[2], fin_free[2];
   uint64_t vsrc_full[2], vsrc_free[2];  // peer sources of a tile, producers -> V warps
   uint32_t tmem_base;
@@ -616,13 +616,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       mbar_init(smem_addr(&ctl.s_full[i]), 1);
       mbar_init(smem_addr(&ctl.s_empty[i]), kPSoftmaxThreads);
       mbar_init(smem_addr(&ctl.m_s_empty[i]), 4);
-      mbar_init(smem_addr(&ctl.xbar[i]), kPSoftmaxThreads);
+      mbar_init(smem_addr(&ctl.xbar[i][0]), 64);
+      mbar_init(smem_addr(&ctl.xbar[i][1]), 64);
       mbar_init(smem_addr(&ctl.fin_full[i]), kPSoftmaxThreads);
       mbar_init(smem_addr(&ctl.fin_free[i]), kPEpiThreads);
     }
     for (int i = 0; i < kValidRing; ++i) {
       mbar_init(smem_addr(&ctl.vfull[i]), 4);
-      mbar_init(smem_addr(&ctl.vfree[i]), 1);
+      mbar_init(smem_addr(&ctl.vfree[i]), 2);  // after each warp pair's exchange
     }
     mbar_init(smem_addr(&ctl.p_full), kPSoftmaxThreads);
     mbar_init(smem_addr(&ctl.m_p_full), 4);
@@ -1062,16 +1063,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         }
         ctl.red[xpar][half][m] = mx;
         if (threadIdx.x == 96) trace_in(tr, 3, 3072, t, 1024);
-        mbar_arrive(smem_addr(&ctl.xbar[xpar]));
-        const bool xw = wait_bar(&ctl, &ctl.xbar[xpar], (xph >> xpar) & 1u, err, 84);
+        // the maximum is exchanged only between the two warps of the same
+        // heads (warps w and w + 2)
+        mbar_arrive(smem_addr(&ctl.xbar[xpar][warp & 1]));
+        const bool xw = wait_bar(&ctl, &ctl.xbar[xpar][warp & 1], (xph >> xpar) & 1u, err, 84);
         xph ^= 1u << xpar;
         if (!__all_sync(0xffffffffu, xw)) {
           ok = false;
           break;
         }
-        // every softmax thread has read valid[vr]: the producers may reuse it
+        // both warps of each pair have read valid[vr]: the producers may
+        // reuse it once both pairs arrived
+        if (threadIdx.x < 64 && lane == 0) mbar_arrive(smem_addr(&ctl.vfree[vr]));
         if (threadIdx.x == 0) {
-          mbar_arrive(smem_addr(&ctl.vfree[vr]));
           trace_in(tr, 2, 0, 4 * t + 1, 4000);
         }
         mx = fmaxf(mx, ctl.red[xpar][half ^ 1][m]);

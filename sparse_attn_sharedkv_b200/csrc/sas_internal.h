@@ -107,12 +107,21 @@ SAS_HD inline QueryKeys query_keys(int32_t scenario, int32_t act_q, int32_t act_
 // Longer rows are cut at tile granularity.
 constexpr int64_t kSnapTiles = 4;
 
+// Cost of a row's key tiles: one unit per 64-key tile; with two head groups
+// (the CTA-pair kernel walks 128-key pair tiles) whole pairs, a half-used
+// last pair costing as much as a full one.
+SAS_HD inline int64_t tiles_cost(int64_t tiles, int32_t head_groups) {
+  return head_groups == 2 ? 2 * ((tiles + 1) / 2) : tiles;
+}
+
 // Point of unit j of a row that starts at `start` on the cost axis and has
 // `tiles` key tiles, doubled to stay integral; a row without tiles is one
-// unit.
-SAS_HD inline int64_t unit_mid2(int64_t start, int64_t tiles, int64_t j) {
+// unit.  With two head groups both tiles of a pair take the pair's
+// midpoint, so pieces of a split row start at even tiles (whole pair tiles).
+SAS_HD inline int64_t unit_mid2(int64_t start, int64_t tiles, int64_t j, int32_t head_groups) {
   if (tiles <= 0) return 2 * start + 1;
-  if (tiles <= kSnapTiles) return 2 * start + 1 + tiles;
+  if (tiles <= kSnapTiles) return 2 * start + 1 + tiles_cost(tiles, head_groups);
+  if (head_groups == 2) return 2 * (start + 1 + 2 * (j >> 1)) + 2;
   return 2 * (start + 1 + j) + 1;
 }
 

@@ -7,8 +7,10 @@
 // 974-1009), rebuilt for 148 SMs: every query token is a row with
 // `window + compressed` key slots (golden.py:125-150); rows are laid out in
 // token order on a cost axis (a fixed per-row cost for the Q load and output
-// store, plus one unit per 64-key tile) and cut into `num_workers` equal
-// spans at tile granularity (rows of at most sas::kSnapTiles tiles whole).  A row whose tiles land on several workers is a
+// store, plus one unit per 64-key tile, rounded up to whole 128-key pair
+// tiles with two head groups) and cut into `num_workers` equal spans at tile
+// granularity (pair-tile granularity with two head groups; rows of at most
+// sas::kSnapTiles tiles whole).  A row whose tiles land on several workers is a
 // split row: each worker writes an fp32 partial (normalised O + LSE) and the
 // combine kernel merges them (the flash-decode reduction the reference plans
 // but never runs).
@@ -89,7 +91,7 @@ int build(const SasProblem& p, int32_t num_sms, bool fill, Built* out) {
   for (int64_t r = 0; r < R; ++r) {
     tiles[r] = (rows[r].slots + sas::kTileKeys - 1) / sas::kTileKeys;
     total_tiles += tiles[r];
-    start[r + 1] = start[r] + kRowCost + tiles[r] * kTileCost;
+    start[r + 1] = start[r] + kRowCost + sas::tiles_cost(tiles[r], hg) * kTileCost;
   }
   const int64_t total = start[R];
   int64_t nw = num_sms / hg;
@@ -111,7 +113,7 @@ int build(const SasProblem& p, int32_t num_sms, bool fill, Built* out) {
     int64_t units = tiles[r] > 0 ? tiles[r] : 1;
     int64_t w_first = -1, w_last = -1, pieces = 0;
     for (int64_t j = 0; j < units; ++j) {
-      const int64_t mid2 = sas::unit_mid2(start[r], tiles[r], j);
+      const int64_t mid2 = sas::unit_mid2(start[r], tiles[r], j, hg);
       int64_t w = owner(mid2);
       if (w_first < 0) w_first = w;
       if (w != w_last) {

@@ -5,8 +5,9 @@
 //
 // Same rows, workers, split rows and partial bases as the host planner for
 // the same lengths (rows carry the same key bounds; the cost axis is 1 per
-// row + 1 per 64-key tile; the owner of a unit is the worker whose share of
-// the cost axis holds the unit's midpoint, sas::unit_mid2).  Only the section offsets differ:
+// row + 1 per 64-key tile, whole pair tiles with two head groups,
+// sas::tiles_cost; the owner of a unit is the worker whose share of the cost
+// axis holds the unit's midpoint, sas::unit_mid2).  Only the section offsets differ:
 // they are fixed by host-known bounds (rows = total_tokens, split rows <=
 // workers - 1, partial slots <= 2 (workers - 1)); the unused split entries
 // carry zero pieces.
@@ -170,7 +171,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       e[sas::R_CMP] = k.cmp; e[sas::R_THR] = k.thr;
     }
     e[sas::R_SLOTS] = slots;
-    my_cost += kRowCost + ((slots + sas::kTileKeys - 1) / sas::kTileKeys) * kTileCost;
+    my_cost += kRowCost +
+               sas::tiles_cost((slots + sas::kTileKeys - 1) / sas::kTileKeys, hg) * kTileCost;
   }
   int64_t my_start;
   const int64_t total = block_exclusive_scan(my_cost, &my_start, scan_smem);
@@ -179,7 +181,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int r = r_lo; r < r_hi; ++r) {
       start[r] = st;
       const int32_t slots = rows[(int64_t)r * sas::kRowInts + sas::R_SLOTS];
-      st += kRowCost + ((slots + sas::kTileKeys - 1) / sas::kTileKeys) * kTileCost;
+      st += kRowCost +
+            sas::tiles_cost((slots + sas::kTileKeys - 1) / sas::kTileKeys, hg) * kTileCost;
     }
   }
   __syncthreads();
@@ -195,13 +198,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     int64_t prev_owner = -1;  // owner of the previous row's last unit
     if (r > 0) {
       const int64_t pt = tiles_of(r - 1);
-      prev_owner = owner_of(unit_mid2(start[r - 1], pt, (pt > 0 ? pt : 1) - 1), nw, total);
+      prev_owner = owner_of(unit_mid2(start[r - 1], pt, (pt > 0 ? pt : 1) - 1, hg), nw, total);
     }
     int64_t next_owner = -1;  // owner of the next row's first unit
-    if (r + 1 < R) next_owner = owner_of(unit_mid2(start[r + 1], tiles_of(r + 1), 0), nw, total);
+    if (r + 1 < R) next_owner = owner_of(unit_mid2(start[r + 1], tiles_of(r + 1), 0, hg), nw, total);
     int64_t w_prev = -1, npieces = 0, w_first = -1;
     for (int64_t j = 0; j < units; ++j) {
-      const int64_t w = owner_of(unit_mid2(start[r], tiles, j), nw, total);
+      const int64_t w = owner_of(unit_mid2(start[r], tiles, j, hg), nw, total);
       if (j == 0) w_first = w;
       const bool new_global = (j == 0) ? (w != prev_owner) : (w != w_prev);
       if (w != w_prev) {
@@ -211,7 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ++npieces;
       }
-      const int64_t wn = (j + 1 < units) ? owner_of(unit_mid2(start[r], tiles, j + 1), nw, total)
+      const int64_t wn = (j + 1 < units) ? owner_of(unit_mid2(start[r], tiles, j + 1, hg), nw, total)
                                          : next_owner;
       if (wn != w) {
         int32_t* e = workers + w * sas::kWorkerInts;
