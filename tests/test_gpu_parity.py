@@ -187,6 +187,11 @@ def test_split_kv_bitwise_stable_per_plan():
          sinks="random"),
     dict(seed=48, layout_q="TND", D=512, d_v=None, scenario=3, q_lens=(4, 2),
          kv_lens=(700, 900), K=128, H=64),
+    # windows of 29..45 keys: the 4-row group at the window / compressed boundary mixes the
+    # two caches (cp.async rows in both kernels)
+    dict(seed=49, layout_q="TND", scenario=3, q_lens=(3, 2), kv_lens=(31, 45), K=32, H=128),
+    dict(seed=50, layout_q="TND", scenario=3, q_lens=(3, 2), kv_lens=(31, 45), K=32, H=64),
+    dict(seed=51, layout_q="TND", scenario=2, ratio=4, q_lens=(3, 2), kv_lens=(31, 45), H=128),
 ])
 def test_edge_cases_vs_oracle(kw):
     case = W.random_case(**kw)

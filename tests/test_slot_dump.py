@@ -153,6 +153,11 @@ CASES = [
     # d_qk 512 and BSND padding
     (dict(seed=412, layout_q="BSND", B=2, H=96, D=512, d_v=None, scenario=3, K=128,
           q_lens=(3, 1), kv_lens=(700, 900)), None, None),
+    # short windows: the 4-row group at the window / compressed boundary mixes the caches
+    (dict(seed=413, layout_q="TND", H=128, scenario=3, K=32, q_lens=(3, 2),
+          kv_lens=(31, 45)), None, None),
+    (dict(seed=414, layout_q="TND", H=64, scenario=3, K=32, q_lens=(3, 2),
+          kv_lens=(31, 45)), None, None),
 ]
 
 
