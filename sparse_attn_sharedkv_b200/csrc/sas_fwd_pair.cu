@@ -30,8 +30,9 @@
 //
 // Every TMA load of both CTAs completes its bytes on the leader's barrier
 // (.cta_group::2 loads, the barrier addressed in CTA 0), and each producer
-// warp of either CTA arrives there once per chunk group with the bytes it
-// issued, so the leader's MMA issuers wait on local barriers only.  The
+// warp (per chunk group) and V warp (per tile) of either CTA arrives there
+// once with the bytes it issued, so the leader's MMA issuers wait on local
+// barriers only.  The
 // leader's tcgen05.commit arrives on the barriers of both CTAs
 // (.multicast::cluster).  CTA 1's softmax and epilogue warps signal P, the
 // S release and the O release with relaxed remote arrivals on mirror
@@ -40,9 +41,10 @@
 //
 // Warp roles in each CTA (512 threads):
 //   0-3    softmax: S from TMEM (thread: one head, one key half of 64 keys),
-//          mask, online softmax seeded by the sink (golden.py:156-196) in the
-//          exp2 domain, P into shared memory, lazy O rescale in TMEM,
-//          statistics of each (row, piece)
+//          mask, maximum exchanged between warps w and w + 2 (the two key
+//          halves of the same heads), online softmax seeded by the sink
+//          (golden.py:156-196) in the exp2 domain, P into shared memory, lazy
+//          O rescale in TMEM, statistics of each (row, piece)
 //   4-7    producers: slot -> (cache, position) -> block table -> row
 //          (golden.py:28-66, kernel.py:2606-2751), validity of the tile's
 //          128 slots, TMA of the CTA's 64 rows (16-row boxes or
@@ -100,7 +102,8 @@ struct PairCtl {
   // Eight arrivals (each producer warp of each CTA, with the bytes of the
   // TMA loads it issued) plus the TMA transactions of both CTAs.
   uint64_t kv_full[2][3];
-  uint64_t v_full[2];                // leader: both CTAs' re-gathered V columns
+  uint64_t v_full[2];                // leader: both CTAs' re-gathered V columns (eight
+                                     // arrivals: each V warp of each CTA, with its bytes)
   uint64_t qk_done[2];               // QK of the stage's tile complete (commit)
   uint64_t pv_done[2];               // PV of the stage's tile complete (commit)
   uint64_t vfull[kValidRing];        // valid bits of tile t in valid[t % 4]
