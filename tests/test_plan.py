@@ -100,6 +100,11 @@ def test_plan_covers_every_tile_once(case, sms):
             assert (r, j) not in seen
             seen[(r, j)] = w
         pieces.setdefault(r, []).append((w, piece))
+        if hg == 2:
+            # the CTA-pair kernel walks 128-key pair tiles: pieces are cut at
+            # whole pairs (even first tile; even end tile unless the row ends)
+            tiles_r = max((rows[r][3] + 63) // 64, 1)
+            assert ja % 2 == 0 and (jb % 2 == 0 or jb == tiles_r), (r, ja, jb)
     for r, row in enumerate(rows):
         units = max((row[3] + 63) // 64, 1)
         assert all((r, j) in seen for j in range(units)), r
